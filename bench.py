@@ -1,0 +1,368 @@
+#!/usr/bin/env python3
+"""SSA attention fwd+bwd benchmark on B200, one process per GPU.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    (N > 1: python -m torch.distributed.run --nproc-per-node N ... bench.py --gpus N ...)
+
+One step = forward + backward of SSA attention over one batch: B=8, Hq=32, Hkv=8, S=2048,
+D=64, bf16, causal, per-head n ~ U(0.3, 0.6), b = 0.8 (seeded synthetic data with the config's
+shapes and value distributions: q, k, v ~ N(0,1)*0.5, dO ~ N(0,1)). FLOPs follow the
+FlashAttention convention, 14*D*E with E = B*Hq*S^2/2 causal score elements (SSA transform
+work is not counted).
+
+Multi-GPU: the (batch, kv-head) units are independent, so each rank owns its own batch of 8
+sequences (weak scaling, global batch 8*N) and the only exchange is one all-reduce of the
+33 floats of dn/db per step. ``value`` = total FLOPs of all ranks / max-over-ranks device time.
+
+Lines printed (rank 0, one JSON line):
+  value     device-resident inputs, timed with CUDA events on the launching stream;
+  e2e       the same metric through the public API with pinned HOST buffers: H2D of
+            q, k, v, dO and D2H of out, dq, dk, dv, dn, db inside the timed region;
+  roofline  the backward call (the dominant launch) against the measured dense bf16 peak;
+  cpu_baseline  the CPU oracle (fp32 eager restatement of the reference's SSA math) timed on
+            this host's cores on a bounded sample (one q-head of one sequence).
+``--impl reference`` times that CPU restatement alone (the reference's own code cannot run on
+the GPU box) and prints its line with "impl": "reference".
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent
+for _p in (str(REPO), str(REPO / "luciole-1b_b200")):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import torch  # noqa: E402
+
+B, HQ, HKV, S, D = 8, 32, 8, 2048, 64
+CAUSAL = True
+SSA_B = 0.8
+WORKLOAD = "config2: SSA causal GQA fwd+bwd, B=8 Hq=32 Hkv=8 S=2048 D=64 bf16, per-head n"
+METRIC = "SSA attn fwd+bwd TFLOP/s (bf16, B=8 Hq=32 Hkv=8 S=2048 D=64 causal)"
+UNIT = "TFLOP/s"
+
+# ncu DRAM traffic (read+write bytes) per launch of the dominant kernel, from the capture
+# summarised in profiles/ (None until captured for the current kernel).
+NCU_TRAFFIC_BYTES = None
+
+
+def flops_per_rank() -> float:
+    E = B * HQ * (S * S // 2 if CAUSAL else S * S)
+    return 14.0 * D * E
+
+
+def flops_bwd_per_rank() -> float:
+    E = B * HQ * (S * S // 2 if CAUSAL else S * S)
+    return 10.0 * D * E
+
+
+def measured_peaks():
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d.get("bf16_tflops", 1590.0), d.get("hbm_gbs", 6650.0), "measured"
+    return 1590.0, 6650.0, "fallback"
+
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML while the timed region runs (reads
+    only; no GPU setting is changed)."""
+
+    REASONS = {
+        0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+        0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+        0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+        0x100: "display_clock_setting",
+    }
+
+    def __init__(self, index: int):
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self._stop = threading.Event()
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nv = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self._nv = None
+        self._t = threading.Thread(target=self._run, daemon=True)
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self._nv.nvmlDeviceGetClockInfo(self._h, self._nv.NVML_CLOCK_SM))
+                r = self._nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                for bit, name in self.REASONS.items():
+                    if r & bit and name != "gpu_idle":
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            self._stop.wait(0.05)
+
+    def __enter__(self):
+        if self._nv is not None:
+            self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self._nv is not None:
+            self._t.join(timeout=1)
+
+    def summary(self):
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None,
+                "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons),
+                "samples": len(self.samples)}
+
+
+def make_inputs(device, seed):
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    q = (torch.randn(B, HQ, S, D, generator=g) * 0.5).to(torch.bfloat16)
+    k = (torch.randn(B, HKV, S, D, generator=g) * 0.5).to(torch.bfloat16)
+    v = (torch.randn(B, HKV, S, D, generator=g) * 0.5).to(torch.bfloat16)
+    do = torch.randn(B, HQ, S, D, generator=g).to(torch.bfloat16)
+    n = 0.3 + 0.3 * torch.rand(HQ, generator=g)
+    return q, k, v, do, n
+
+
+def cpu_oracle_sample(threads: int):
+    """Time the CPU restatement of the reference's eager SSA path (fp32, autograd) on one q-head
+    of one sequence at S=2048; returns (TFLOP/s, seconds, flops)."""
+    from oracle.ssa_oracle import ssa_reference_grads
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(123)
+    q = torch.randn(1, 1, S, D, generator=g) * 0.5
+    k = torch.randn(1, 1, S, D, generator=g) * 0.5
+    v = torch.randn(1, 1, S, D, generator=g) * 0.5
+    do = torch.randn(1, 1, S, D, generator=g)
+    n, b = torch.tensor(0.43), torch.tensor(SSA_B)
+    flops = 14.0 * D * (S * S // 2)
+    ssa_reference_grads(q, k, v, D ** -0.5, n, b, do, CAUSAL, compute_dtype=torch.float32)  # warm
+    reps, t0 = 0, time.perf_counter()
+    while True:
+        ssa_reference_grads(q, k, v, D ** -0.5, n, b, do, CAUSAL, compute_dtype=torch.float32)
+        reps += 1
+        el = time.perf_counter() - t0
+        if el > 10.0 or reps >= 50:
+            break
+    return flops * reps / el / 1e12, el, flops * reps, reps
+
+
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def run_reference(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    threads = os.cpu_count() or 1
+    vals = []
+    for i in range(args.warmup + args.steps):
+        v, _, _, _ = _one_ref_step(threads)
+        if i >= args.warmup:
+            vals.append(v)
+    val = statistics.median(vals)
+    sample = (f"one q-head of one sequence (S={S}, D={D}, causal) per step, fp32 eager "
+              f"restatement of the reference's SSA path with autograd")
+    line = {"impl": "reference", "metric": METRIC, "value": val, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "global_batch": B * world, "seq_len": S},
+            "cpu_baseline": {"value": val, "unit": UNIT, "cores": threads, "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": val, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def _one_ref_step(threads):
+    from oracle.ssa_oracle import ssa_reference_grads
+    torch.set_num_threads(threads)
+    g = torch.Generator().manual_seed(7)
+    q = torch.randn(1, 1, S, D, generator=g) * 0.5
+    k = torch.randn(1, 1, S, D, generator=g) * 0.5
+    v = torch.randn(1, 1, S, D, generator=g) * 0.5
+    do = torch.randn(1, 1, S, D, generator=g)
+    t0 = time.perf_counter()
+    ssa_reference_grads(q, k, v, D ** -0.5, torch.tensor(0.43), torch.tensor(SSA_B), do, CAUSAL,
+                        compute_dtype=torch.float32)
+    el = time.perf_counter() - t0
+    fl = 14.0 * D * (S * S // 2)
+    return fl / el / 1e12, el, fl, 1
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    if args.impl == "reference":
+        run_reference(args)
+        return
+
+    world, rank, local = dist_setup(args)
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    from SSA import _lib
+    from SSA.ssa_triton_kernel import ssa_flash_attn_backward, ssa_flash_attn_forward
+    import torch.distributed as dist
+
+    q_h, k_h, v_h, do_h, n_h = make_inputs(dev, seed=rank)
+    q, k, v, do = (t.to(dev) for t in (q_h, k_h, v_h, do_h))
+    n = n_h.to(dev)
+    bb = torch.tensor(SSA_B, device=dev)
+    scale = D ** -0.5
+    red = torch.zeros(HQ + 1, device=dev)
+
+    def step():
+        out, m = ssa_flash_attn_forward(q, k, v, scale, n, bb, causal=CAUSAL)
+        dq, dk, dv, dn, db = ssa_flash_attn_backward(q, k, v, out, do, m, scale, n, bb, causal=CAUSAL)
+        if world > 1:
+            red[:HQ].copy_(dn)
+            red[HQ:].copy_(db.reshape(1))
+            dist.all_reduce(red)
+        return out, dq, dk, dv, dn, db
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize(dev)
+
+    for _ in range(args.warmup):
+        step()
+    barrier()
+
+    # ---- value: device-resident inputs; per-call events for the roofline
+    st = torch.cuda.current_stream(dev)
+    launches0 = _lib.launch_count()
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
+           torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        barrier()
+        start.record(st)
+        for i in range(args.steps):
+            e0, e1, e2 = ev[i]
+            e0.record(st)
+            out, m = ssa_flash_attn_forward(q, k, v, scale, n, bb, causal=CAUSAL)
+            e1.record(st)
+            dq, dk, dv, dn, db = ssa_flash_attn_backward(q, k, v, out, do, m, scale, n, bb,
+                                                         causal=CAUSAL)
+            e2.record(st)
+            if world > 1:
+                red[:HQ].copy_(dn)
+                red[HQ:].copy_(db.reshape(1))
+                dist.all_reduce(red)
+        stop.record(st)
+        barrier()
+    launches = _lib.launch_count() - launches0
+    ms = start.elapsed_time(stop) / args.steps
+    t_fwd = statistics.median(a.elapsed_time(b) for a, b, _ in ev)
+    t_bwd = statistics.median(b.elapsed_time(c) for _, b, c in ev)
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    value = flops_per_rank() * world / (ms * 1e-3) / 1e12
+
+    # ---- e2e: through the public API with pinned host buffers, copies inside the timed region
+    q_p, k_p, v_p, do_p = (t.pin_memory() for t in (q_h, k_h, v_h, do_h))
+    outs_p = [torch.empty(q_h.shape, dtype=torch.bfloat16).pin_memory() for _ in range(2)] + \
+             [torch.empty(k_h.shape, dtype=torch.bfloat16).pin_memory() for _ in range(2)] + \
+             [torch.empty(HQ + 1, dtype=torch.float32).pin_memory()]
+    h2d = sum(t.numel() * t.element_size() for t in (q_p, k_p, v_p, do_p))
+    d2h = sum(t.numel() * t.element_size() for t in outs_p)
+    e2e_steps = max(3, min(args.steps, 20))
+
+    def e2e_step():
+        qd, kd, vd, dod = (t.to(dev, non_blocking=True) for t in (q_p, k_p, v_p, do_p))
+        out_, m_ = ssa_flash_attn_forward(qd, kd, vd, scale, n, bb, causal=CAUSAL)
+        dq_, dk_, dv_, dn_, db_ = ssa_flash_attn_backward(qd, kd, vd, out_, dod, m_, scale, n, bb,
+                                                          causal=CAUSAL)
+        red[:HQ].copy_(dn_)
+        red[HQ:].copy_(db_.reshape(1))
+        if world > 1:
+            dist.all_reduce(red)
+        for dst, src in zip(outs_p, (out_, dq_, dk_, dv_, red)):
+            dst.copy_(src, non_blocking=True)
+
+    e2e_step()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(st)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(st)
+    barrier()
+    e2e_ms = e0.elapsed_time(e1) / e2e_steps
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    e2e_val = flops_per_rank() * world / (e2e_ms * 1e-3) / 1e12
+
+    status = _lib.load().ssa_device_status(_lib.stream_ptr(dev))
+    peak_tf, _, peak_kind = measured_peaks()
+    achieved = flops_bwd_per_rank() / (t_bwd * 1e-3) / 1e12
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        threads = os.cpu_count() or 1
+        v_cpu, el, _, reps = cpu_oracle_sample(threads)
+        cpu = {"value": v_cpu, "unit": UNIT, "cores": threads, "kind": "port",
+               "sample": f"{reps} x fwd+bwd of one q-head of one sequence (S={S}, D={D}, causal), "
+                         f"fp32 eager oracle with autograd, {el:.1f} s"}
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "global_batch": B * world, "seq_len": S,
+                       "heads_q": HQ, "heads_kv": HKV, "head_dim": D, "causal": CAUSAL,
+                       "parallelism": f"batch-shard x{world} (weak), dn/db all-reduce",
+                       "l2": "inputs larger than L2 (~300 MB resident per rank)"},
+            "fwd_ms": t_fwd, "bwd_ms": t_bwd,
+            "frac_of_peak": value / world / peak_tf,
+            "e2e": {"value": e2e_val, "unit": UNIT, "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
+            "roofline": {"bound": "tensor", "kernel": "ssa_attn_bwd call (dominant)",
+                         "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
+                         "frac": achieved / peak_tf, "peak_kind": f"{peak_kind} bf16 burst",
+                         "traffic": NCU_TRAFFIC_BYTES},
+            "cpu_baseline": cpu,
+            "clocks": clk.summary(),
+            "gpu_launches": launches,
+            "device_status": status,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

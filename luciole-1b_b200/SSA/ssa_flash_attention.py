@@ -1,0 +1,101 @@
+"""Differentiable SSA flash attention over libssa_b200.so.
+
+Drop-in for the reference ``SSA.ssa_flash_attention``
+(training/train/train_ssa_triton/SSA/ssa_flash_attention.py): ``SSAFlashAttnFunc`` takes the
+same 9 positional arguments and its backward returns 9 gradients in the same order
+(``dq, dk, dv, None, dn, db, None, None, None``, reference :66). Saved state is q, k, v, out,
+m and the fp32 parameters (reference :43); no O(N^2) tensor is kept.
+
+``SSAVarlenFlashAttnFunc`` / ``ssa_flash_attn_varlen_func`` add packed documents
+(``cu_seqlens``), which the reference does not support.
+"""
+
+from __future__ import annotations
+
+import torch
+from torch.autograd import Function
+
+from .ssa_triton_kernel import (
+    ssa_flash_attn_backward,
+    ssa_flash_attn_forward,
+    ssa_flash_attn_varlen_backward,
+    ssa_flash_attn_varlen_forward,
+)
+
+__all__ = ["SSAFlashAttnFunc", "ssa_flash_attention", "SSAVarlenFlashAttnFunc",
+           "ssa_flash_attn_varlen_func"]
+
+
+def _grad_like(g: torch.Tensor, ref: torch.Tensor) -> torch.Tensor:
+    g = g.reshape(ref.shape)
+    return g if g.dtype == ref.dtype else g.to(ref.dtype)
+
+
+class SSAFlashAttnFunc(Function):
+    """out = softmax(n * sign(s) * log1p(b |s|)) @ V with s = scale * Q K^T (causal optional)."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, softmax_scale, ssa_n, ssa_b, causal, dropout_p, training):
+        ssa_n_f32 = ssa_n.float().contiguous()
+        ssa_b_f32 = ssa_b.float().contiguous()
+        out, m = ssa_flash_attn_forward(q, k, v, softmax_scale, ssa_n_f32, ssa_b_f32, causal)
+        ctx.save_for_backward(q, k, v, out, m, ssa_n_f32, ssa_b_f32)
+        ctx.softmax_scale = softmax_scale
+        ctx.causal = causal
+        ctx.dropout_p = dropout_p
+        ctx.n_meta = (ssa_n.shape, ssa_n.dtype)
+        ctx.b_meta = (ssa_b.shape, ssa_b.dtype)
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        q, k, v, out, m, ssa_n_f32, ssa_b_f32 = ctx.saved_tensors
+        dout = dout.contiguous()
+        dq, dk, dv, dn, db = ssa_flash_attn_backward(
+            q, k, v, out, dout, m, ctx.softmax_scale, ssa_n_f32, ssa_b_f32, ctx.causal)
+        dn = dn.reshape(ctx.n_meta[0]).to(ctx.n_meta[1])
+        db = db.reshape(ctx.b_meta[0]).to(ctx.b_meta[1])
+        return dq, dk, dv, None, dn, db, None, None, None
+
+
+def ssa_flash_attention(q, k, v, softmax_scale, ssa_n, ssa_b, causal=True, dropout_p=0.0,
+                        training=True):
+    """High-level API (reference ssa_flash_attention.py:69-97): q [B, Hq, N, D],
+    k/v [B, Hkv, N, D] (native GQA), ssa_n 0-d or [Hq], ssa_b 0-d. Returns [B, Hq, N, D]."""
+    return SSAFlashAttnFunc.apply(q, k, v, softmax_scale, ssa_n, ssa_b, causal, dropout_p,
+                                  training)
+
+
+class SSAVarlenFlashAttnFunc(Function):
+    """Packed-document SSA attention: q [T, Hq, D], k/v [T, Hkv, D], cu_seqlens int32."""
+
+    @staticmethod
+    def forward(ctx, q, k, v, cu_seqlens, max_seqlen, softmax_scale, ssa_n, ssa_b, causal):
+        ssa_n_f32 = ssa_n.float().contiguous()
+        ssa_b_f32 = ssa_b.float().contiguous()
+        out, lse = ssa_flash_attn_varlen_forward(q, k, v, cu_seqlens, max_seqlen, softmax_scale,
+                                                 ssa_n_f32, ssa_b_f32, causal)
+        ctx.save_for_backward(q, k, v, out, lse, cu_seqlens, ssa_n_f32, ssa_b_f32)
+        ctx.max_seqlen = max_seqlen
+        ctx.softmax_scale = softmax_scale
+        ctx.causal = causal
+        ctx.n_meta = (ssa_n.shape, ssa_n.dtype)
+        ctx.b_meta = (ssa_b.shape, ssa_b.dtype)
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        q, k, v, out, lse, cu, n32, b32 = ctx.saved_tensors
+        dq, dk, dv, dn, db = ssa_flash_attn_varlen_backward(
+            q, k, v, out, dout.contiguous(), lse, cu, ctx.max_seqlen, ctx.softmax_scale, n32, b32,
+            ctx.causal)
+        dn = dn.reshape(ctx.n_meta[0]).to(ctx.n_meta[1])
+        db = db.reshape(ctx.b_meta[0]).to(ctx.b_meta[1])
+        return dq, dk, dv, None, None, None, dn, db, None
+
+
+def ssa_flash_attn_varlen_func(q, k, v, cu_seqlens, max_seqlen, softmax_scale, ssa_n, ssa_b,
+                               causal=True):
+    """Packed documents (THD + cu_seqlens); each document attends only within itself."""
+    return SSAVarlenFlashAttnFunc.apply(q, k, v, cu_seqlens, int(max_seqlen), softmax_scale,
+                                        ssa_n, ssa_b, causal)

@@ -1,0 +1,254 @@
+"""SSA flash-attention forward / backward wrappers over libssa_b200.so.
+
+Drop-in for the reference module ``SSA.ssa_triton_kernel``
+(training/train/train_ssa_triton/SSA/ssa_triton_kernel.py): same function names, argument
+meaning and return values, computed by hand-written sm_100a CUDA (tcgen05/TMA for bf16/fp16
+with D in {64, 128}; fp32-arithmetic CUDA-core kernels for fp32 and other head dims). The
+module name is kept so ``from SSA.ssa_triton_kernel import ...`` keeps working; nothing here
+uses Triton.
+
+Differences from the reference, all supersets:
+  * ``ssa_n`` may be 0-d (reference) or a per-head ``[Hq]`` vector; ``dn`` takes its shape.
+  * N need not be a multiple of 128 (reference asserts it in backward, :852-857) and D may be
+    16 / 32 / 64 / 128 (reference: any power of two its Triton build handles).
+  * packed documents: ``ssa_flash_attn_varlen_forward/backward`` (reference asserts packed
+    sequences off, ssa_triton_attention.py:154-156).
+  * ``m`` is the same base-2 normaliser M = log2(sum_j exp2(t_j log2 e)) (:248-255).
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+from typing import Optional, Tuple
+
+import torch
+
+from . import _lib
+
+__all__ = [
+    "ssa_flash_attn_forward", "ssa_flash_attn_backward", "ssa_flash_attn_varlen_forward",
+    "ssa_flash_attn_varlen_backward", "warmup_ssa_triton_kernels", "kernel_family",
+]
+
+
+def _params(ssa_n: torch.Tensor, ssa_b: torch.Tensor, hq: int, device) -> Tuple[torch.Tensor, torch.Tensor, int]:
+    n = torch.as_tensor(ssa_n).detach().to(device=device, dtype=torch.float32).contiguous()
+    b = torch.as_tensor(ssa_b).detach().to(device=device, dtype=torch.float32).contiguous()
+    if b.numel() != 1:
+        raise ValueError(f"ssa_b must be a scalar tensor, got shape {tuple(b.shape)}")
+    if n.numel() == 1:
+        per_head = 0
+    elif n.numel() == hq:
+        per_head = 1
+    else:
+        raise ValueError(f"ssa_n must be a scalar or have Hq={hq} elements, got {tuple(n.shape)}")
+    return n, b, per_head
+
+
+def _problem(q: torch.Tensor, hkv: int, softmax_scale: float, n: torch.Tensor, b: torch.Tensor,
+             per_head: int, causal: bool, B: int, N: int,
+             cu_seqlens: Optional[torch.Tensor] = None, max_seqlen: int = 0) -> _lib.SsaProblem:
+    if q.dtype not in _lib.DTYPE_CODES:
+        raise ValueError(f"unsupported dtype {q.dtype}")
+    hq, d = q.shape[1], q.shape[-1]
+    return _lib.SsaProblem(
+        _lib.DTYPE_CODES[q.dtype], B, hq, hkv, N, d, 1 if causal else 0, float(softmax_scale),
+        n.data_ptr(), per_head, b.data_ptr(),
+        cu_seqlens.data_ptr() if cu_seqlens is not None else None, int(max_seqlen))
+
+
+def _tma_ok(t: torch.Tensor) -> bool:
+    if t.stride(-1) != 1 or t.data_ptr() % 16:
+        return False
+    return all((s * t.element_size()) % 16 == 0 for s, n in zip(t.stride()[:-1], t.shape[:-1]) if n > 1)
+
+
+def _prep(t: torch.Tensor, family: int) -> torch.Tensor:
+    """Unit stride on D always; 16-byte-aligned strides for the TMA (tensor-core) family."""
+    if t.stride(-1) != 1 or (family == 1 and not _tma_ok(t)):
+        return t.contiguous()
+    return t
+
+
+def _check_qkv(q, k, v):
+    if q.dim() != 4 or k.dim() != 4 or v.dim() != 4:
+        raise ValueError("q, k, v must be [B, H, N, D]")
+    if not (q.is_cuda and k.is_cuda and v.is_cuda):
+        raise ValueError("q, k, v must be CUDA tensors (there is no CPU path)")
+    if not (q.dtype == k.dtype == v.dtype):
+        raise ValueError(f"dtype mismatch q={q.dtype} k={k.dtype} v={v.dtype}")
+    B, Hq, N, D = q.shape
+    if k.shape != v.shape or k.shape[0] != B or k.shape[2] != N or k.shape[3] != D:
+        raise ValueError(f"shape mismatch q={tuple(q.shape)} k={tuple(k.shape)} v={tuple(v.shape)}")
+    Hkv = k.shape[1]
+    if Hq % Hkv != 0:
+        raise ValueError(f"Hq={Hq} must be divisible by Hkv={Hkv}")
+    return B, Hq, Hkv, N, D
+
+
+def kernel_family(q: torch.Tensor, softmax_scale: float = 1.0) -> int:
+    """0 = generic fp32-arithmetic kernels, 1 = sm_100a tcgen05/TMA kernels."""
+    D = q.shape[-1]
+    n = torch.zeros(1, device=q.device)
+    prob = _lib.SsaProblem(_lib.DTYPE_CODES[q.dtype], 1, 1, 1, 1, D, 1, float(softmax_scale),
+                           n.data_ptr(), 0, n.data_ptr(), None, 0)
+    return _lib.load().ssa_attn_kernel_family(ctypes.byref(prob))
+
+
+def ssa_flash_attn_forward(q, k, v, softmax_scale, ssa_n, ssa_b, causal=True):
+    """Forward (reference ssa_triton_kernel.py:732-792).
+
+    q [B, Hq, N, D], k/v [B, Hkv, N, D] (any strides with a unit D stride; other layouts
+    are copied). Returns (out [B, Hq, N, D] with q's dtype and layout, m [B, Hq, N] fp32).
+    """
+    lib = _lib.load()
+    B, Hq, Hkv, N, D = _check_qkv(q, k, v)
+    n, b, per_head = _params(ssa_n, ssa_b, Hq, q.device)
+    prob = _problem(q, Hkv, softmax_scale, n, b, per_head, causal, B, N)
+    fam = lib.ssa_attn_kernel_family(ctypes.byref(prob))
+    q, k, v = _prep(q, fam), _prep(k, fam), _prep(v, fam)
+    out = torch.empty_like(q)
+    if fam == 1 and not _tma_ok(out):
+        out = torch.empty(q.shape, dtype=q.dtype, device=q.device)
+    m = torch.empty((B, Hq, N), device=q.device, dtype=torch.float32)
+    with torch.cuda.device(q.device):
+        rc = lib.ssa_attn_fwd(ctypes.byref(prob), _lib.tensor_bhnd(q), _lib.tensor_bhnd(k),
+                              _lib.tensor_bhnd(v), _lib.tensor_bhnd(out), m.data_ptr(), None, 0,
+                              _lib.stream_ptr(q.device))
+    _lib.check(rc)
+    return out, m
+
+
+def ssa_flash_attn_backward(q, k, v, out, dout, m, softmax_scale, ssa_n, ssa_b, causal=True):
+    """Backward (reference ssa_triton_kernel.py:795-897).
+
+    Returns (dq, dk, dv, dn, db): dq/dk/dv in the inputs' dtype and layout; dn fp32 with
+    ssa_n's shape (0-d in the reference); db a 0-d fp32 tensor. dn/db are reduced on the
+    device (fp64, deterministic); no host synchronisation happens.
+    """
+    lib = _lib.load()
+    B, Hq, Hkv, N, D = _check_qkv(q, k, v)
+    n, b, per_head = _params(ssa_n, ssa_b, Hq, q.device)
+    prob = _problem(q, Hkv, softmax_scale, n, b, per_head, causal, B, N)
+    fam = lib.ssa_attn_kernel_family(ctypes.byref(prob))
+    q, k, v, dout = _prep(q, fam), _prep(k, fam), _prep(v, fam), _prep(dout, fam)
+    out = out if out.stride(-1) == 1 else out.contiguous()
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    dn = torch.empty(n.shape, device=q.device, dtype=torch.float32)
+    db = torch.empty((), device=q.device, dtype=torch.float32)
+    ws_bytes = lib.ssa_attn_bwd_workspace_size(ctypes.byref(prob))
+    ws = torch.empty(max(ws_bytes, 1), device=q.device, dtype=torch.uint8)
+    with torch.cuda.device(q.device):
+        rc = lib.ssa_attn_bwd(ctypes.byref(prob), _lib.tensor_bhnd(q), _lib.tensor_bhnd(k),
+                              _lib.tensor_bhnd(v), _lib.tensor_bhnd(out), _lib.tensor_bhnd(dout),
+                              m.data_ptr(), _lib.tensor_bhnd(dq), _lib.tensor_bhnd(dk),
+                              _lib.tensor_bhnd(dv), dn.data_ptr(), db.data_ptr(), ws.data_ptr(),
+                              ws_bytes, _lib.stream_ptr(q.device))
+    _lib.check(rc)
+    if tuple(dn.shape) != tuple(torch.as_tensor(ssa_n).shape):
+        dn = dn.reshape(torch.as_tensor(ssa_n).shape)
+    return dq, dk, dv, dn, db
+
+
+# ------------------------------------------------------------------------------ varlen
+def _check_thd(q, k, v, cu_seqlens):
+    if q.dim() != 3 or k.dim() != 3 or v.dim() != 3:
+        raise ValueError("varlen q, k, v must be [T, H, D]")
+    if not (q.is_cuda and k.is_cuda and v.is_cuda and cu_seqlens.is_cuda):
+        raise ValueError("varlen tensors must be CUDA tensors (there is no CPU path)")
+    if cu_seqlens.dtype != torch.int32 or cu_seqlens.dim() != 1 or cu_seqlens.numel() < 2:
+        raise ValueError("cu_seqlens must be a 1-D int32 tensor with ndoc+1 entries")
+    T, Hq, D = q.shape
+    if k.shape != v.shape or k.shape[0] != T or k.shape[2] != D:
+        raise ValueError(f"shape mismatch q={tuple(q.shape)} k={tuple(k.shape)}")
+    if Hq % k.shape[1] != 0:
+        raise ValueError(f"Hq={Hq} must be divisible by Hkv={k.shape[1]}")
+    return T, Hq, k.shape[1], D, cu_seqlens.numel() - 1
+
+
+def _prep3(t, fam):
+    if t.stride(-1) != 1 or (fam == 1 and not _tma_ok(t)):
+        return t.contiguous()
+    return t
+
+
+def ssa_flash_attn_varlen_forward(q, k, v, cu_seqlens, max_seqlen, softmax_scale, ssa_n, ssa_b,
+                                  causal=True):
+    """Packed documents: q [T, Hq, D], k/v [T, Hkv, D], cu_seqlens int32 [ndoc+1].
+
+    Each document attends only within itself (causal or not). Returns (out [T, Hq, D],
+    lse [Hq, T] fp32). No reference counterpart: the reference asserts packed sequences off
+    (ssa_triton_attention.py:154-156).
+    """
+    lib = _lib.load()
+    T, Hq, Hkv, D, ndoc = _check_thd(q, k, v, cu_seqlens)
+    n, b, per_head = _params(ssa_n, ssa_b, Hq, q.device)
+    prob = _lib.SsaProblem(_lib.DTYPE_CODES[q.dtype], ndoc, Hq, Hkv, T, D, 1 if causal else 0,
+                           float(softmax_scale), n.data_ptr(), per_head, b.data_ptr(),
+                           cu_seqlens.data_ptr(), int(max_seqlen))
+    fam = lib.ssa_attn_kernel_family(ctypes.byref(prob))
+    q, k, v = _prep3(q, fam), _prep3(k, fam), _prep3(v, fam)
+    out = torch.empty(q.shape, dtype=q.dtype, device=q.device)
+    lse = torch.empty((Hq, T), device=q.device, dtype=torch.float32)
+    with torch.cuda.device(q.device):
+        rc = lib.ssa_attn_fwd(ctypes.byref(prob), _lib.tensor_thd(q), _lib.tensor_thd(k),
+                              _lib.tensor_thd(v), _lib.tensor_thd(out), lse.data_ptr(), None, 0,
+                              _lib.stream_ptr(q.device))
+    _lib.check(rc)
+    return out, lse
+
+
+def ssa_flash_attn_varlen_backward(q, k, v, out, dout, lse, cu_seqlens, max_seqlen,
+                                   softmax_scale, ssa_n, ssa_b, causal=True):
+    """Backward of :func:`ssa_flash_attn_varlen_forward`. Returns (dq, dk, dv, dn, db)."""
+    lib = _lib.load()
+    T, Hq, Hkv, D, ndoc = _check_thd(q, k, v, cu_seqlens)
+    n, b, per_head = _params(ssa_n, ssa_b, Hq, q.device)
+    prob = _lib.SsaProblem(_lib.DTYPE_CODES[q.dtype], ndoc, Hq, Hkv, T, D, 1 if causal else 0,
+                           float(softmax_scale), n.data_ptr(), per_head, b.data_ptr(),
+                           cu_seqlens.data_ptr(), int(max_seqlen))
+    fam = lib.ssa_attn_kernel_family(ctypes.byref(prob))
+    q, k, v, dout = _prep3(q, fam), _prep3(k, fam), _prep3(v, fam), _prep3(dout, fam)
+    out = out if out.stride(-1) == 1 else out.contiguous()
+    dq = torch.empty(q.shape, dtype=q.dtype, device=q.device)
+    dk = torch.empty(k.shape, dtype=k.dtype, device=k.device)
+    dv = torch.empty(v.shape, dtype=v.dtype, device=v.device)
+    dn = torch.empty(n.shape, device=q.device, dtype=torch.float32)
+    db = torch.empty((), device=q.device, dtype=torch.float32)
+    ws_bytes = lib.ssa_attn_bwd_workspace_size(ctypes.byref(prob))
+    ws = torch.empty(max(ws_bytes, 1), device=q.device, dtype=torch.uint8)
+    with torch.cuda.device(q.device):
+        rc = lib.ssa_attn_bwd(ctypes.byref(prob), _lib.tensor_thd(q), _lib.tensor_thd(k),
+                              _lib.tensor_thd(v), _lib.tensor_thd(out), _lib.tensor_thd(dout),
+                              lse.data_ptr(), _lib.tensor_thd(dq), _lib.tensor_thd(dk),
+                              _lib.tensor_thd(dv), dn.data_ptr(), db.data_ptr(), ws.data_ptr(),
+                              ws_bytes, _lib.stream_ptr(q.device))
+    _lib.check(rc)
+    if tuple(dn.shape) != tuple(torch.as_tensor(ssa_n).shape):
+        dn = dn.reshape(torch.as_tensor(ssa_n).shape)
+    return dq, dk, dv, dn, db
+
+
+def warmup_ssa_triton_kernels(B: int = 2, Hq: int = 24, Hkv: int = 8, N: int = 128, D: int = 32,
+                              dtype: torch.dtype = torch.bfloat16, device: str = "cuda"):
+    """Run one tiny forward + backward (reference ssa_triton_kernel.py:904-928).
+
+    Nothing is JIT-compiled here (the kernels are built ahead of time); this loads the
+    library, creates the CUDA module and resolves the TMA encoder. The RNG state is restored.
+    """
+    state = torch.cuda.get_rng_state(device) if torch.cuda.is_available() else None
+    try:
+        q = torch.randn(B, Hq, N, D, dtype=dtype, device=device)
+        k = torch.randn(B, Hkv, N, D, dtype=dtype, device=device)
+        v = torch.randn(B, Hkv, N, D, dtype=dtype, device=device)
+        ssa_n = torch.tensor(1.5, dtype=torch.float32, device=device)
+        ssa_b = torch.tensor(0.8, dtype=torch.float32, device=device)
+        scale = 1.0 / math.sqrt(D)
+        out, m = ssa_flash_attn_forward(q, k, v, scale, ssa_n, ssa_b, causal=True)
+        dout = torch.randn_like(out)
+        ssa_flash_attn_backward(q, k, v, out, dout, m, scale, ssa_n, ssa_b, causal=True)
+        torch.cuda.synchronize(device)
+    finally:
+        if state is not None:
+            torch.cuda.set_rng_state(state, device)

@@ -1,0 +1,97 @@
+// ssa_common.cuh — parameter blocks, dtype helpers and the SSA logit transform shared by
+// the generic (SIMT) and the sm_100a (tcgen05/TMA) kernels.
+//
+// The SSA transform (reference: training/train/train_ssa_triton/SSA/ssa_triton_kernel.py:96-107):
+//     s  = softmax_scale * (q . k)
+//     u  = b * |s|
+//     t  = n * sign(s) * log1p(u)
+//     t2 = t * log2(e)                      (base-2 online normaliser, :107-113)
+// Backward chain rule (:378-397):
+//     ds_ssa = P * (dP - Delta)
+//     dL/ds  = ds_ssa * n * b / (1 + u)
+//     dn    += ds_ssa * sign(s) * log1p(u)
+//     db    += ds_ssa * n * sign(s) * |s| / (1 + u)  ( = ds_ssa * n * s / (1 + u) )
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include "ssa_b200.h"
+
+namespace ssa {
+
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+
+// Device-side problem block (plain data, passed by value to every kernel).
+struct Problem {
+  int B, Hq, Hkv, N, D, gqa;
+  int causal;
+  float scale;
+  const float* n_ptr;
+  int n_per_head;
+  const float* b_ptr;
+  const int* cu_seqlens;  // nullptr: dense
+  int max_seqlen;         // rows a sequence can have (N when dense)
+};
+
+struct TensorRef {
+  void* ptr;
+  int64_t sB, sH, sN;
+};
+
+// Start row and length of sequence z (a batch entry, or a document when varlen).
+__device__ __forceinline__ void seq_bounds(const Problem& p, int z, int& start, int& len) {
+  if (p.cu_seqlens) {
+    start = __ldg(p.cu_seqlens + z);
+    len = __ldg(p.cu_seqlens + z + 1) - start;
+  } else {
+    start = 0;
+    len = p.N;
+  }
+}
+
+// Element offset of (z, h, row) in a strided tensor; row is relative to the sequence start.
+__device__ __forceinline__ int64_t row_offset(const TensorRef& t, const Problem& p, int z, int h,
+                                              int seq_start, int row) {
+  const int64_t zb = p.cu_seqlens ? 0 : (int64_t)z * t.sB;
+  return zb + (int64_t)h * t.sH + (int64_t)(seq_start + row) * t.sN;
+}
+
+// Offset into a [B, Hq, N] (dense) or [Hq, T] (varlen) fp32 row-statistics array (lse, delta).
+__device__ __forceinline__ int64_t stat_offset(const Problem& p, int z, int h, int seq_start,
+                                               int row) {
+  if (p.cu_seqlens) return (int64_t)h * p.N + seq_start + row;  // N == T (total tokens)
+  return ((int64_t)z * p.Hq + h) * p.N + row;
+}
+
+__device__ __forceinline__ float load_n(const Problem& p, int hq) {
+  return __ldg(p.n_ptr + (p.n_per_head ? hq : 0));
+}
+
+template <typename T> __device__ __forceinline__ float to_f32(T x);
+template <> __device__ __forceinline__ float to_f32<float>(float x) { return x; }
+template <> __device__ __forceinline__ float to_f32<__half>(__half x) { return __half2float(x); }
+template <> __device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 x) {
+  return __bfloat162float(x);
+}
+
+template <typename T> __device__ __forceinline__ T from_f32(float x);
+template <> __device__ __forceinline__ float from_f32<float>(float x) { return x; }
+template <> __device__ __forceinline__ __half from_f32<__half>(float x) { return __float2half_rn(x); }
+template <> __device__ __forceinline__ __nv_bfloat16 from_f32<__nv_bfloat16>(float x) {
+  return __float2bfloat16_rn(x);
+}
+
+// Accurate transform used by the generic path (fp32 inputs need 1e-5 relative parity):
+// returns sign(s)*log1p(b|s|) (natural log) and 1/(1+b|s|) through out-params.
+__device__ __forceinline__ float ssa_signed_log1p(float s, float b, float& inv_1pu) {
+  const float u = b * fabsf(s);
+  inv_1pu = 1.0f / (1.0f + u);
+  const float l = log1pf(u);
+  return s > 0.f ? l : (s < 0.f ? -l : 0.f);
+}
+
+}  // namespace ssa

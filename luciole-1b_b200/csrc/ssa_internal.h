@@ -1,0 +1,39 @@
+// ssa_internal.h — launchers shared between the C ABI (ssa_capi.cu) and the kernel files.
+#pragma once
+
+#include "ssa_common.cuh"
+
+namespace ssa {
+
+// Generic fp32-compute kernels (ssa_generic.cu).
+bool generic_supports_head_dim(int D);
+int generic_bwd_partials_per_seq(const Problem& p);
+int launch_fwd_generic(int dtype, const Problem& p, TensorRef q, TensorRef k, TensorRef v,
+                       TensorRef o, float* lse, cudaStream_t st);
+int launch_bwd_preprocess(int dtype, const Problem& p, TensorRef o, TensorRef dout, float* delta,
+                          cudaStream_t st);
+int launch_bwd_generic(int dtype, const Problem& p, TensorRef q, TensorRef k, TensorRef v,
+                       TensorRef dout, const float* lse, const float* delta, TensorRef dq,
+                       TensorRef dk, TensorRef dv, float* dn_part, float* db_part,
+                       cudaStream_t st);
+int launch_dndb_reduce(const float* dn_part, const float* db_part, int Z, int Hq, int P,
+                       int n_per_head, float* dn, float* db, cudaStream_t st);
+
+// sm_100a tcgen05 / TMA kernels (ssa_sm100_fwd.cu, ssa_sm100_bwd.cu).
+bool sm100_supports(int dtype, int D);
+int launch_fwd_sm100(int dtype, const Problem& p, TensorRef q, TensorRef k, TensorRef v,
+                     TensorRef o, float* lse, cudaStream_t st);
+bool sm100_bwd_supports(int dtype, int D);
+size_t sm100_bwd_workspace_bytes(const Problem& p);
+int launch_bwd_sm100(int dtype, const Problem& p, TensorRef q, TensorRef k, TensorRef v,
+                     TensorRef dout, const float* lse, const float* delta, TensorRef dq,
+                     TensorRef dk, TensorRef dv, float* dn, float* db, void* ws, size_t ws_bytes,
+                     cudaStream_t st);
+
+// Device status word written by bounded waits in the sm_100a kernels.
+unsigned int* device_status_ptr();
+
+// Host-side count of kernel launches issued by this library (ssa_kernel_launch_count).
+void note_launches(int n);
+
+}  // namespace ssa

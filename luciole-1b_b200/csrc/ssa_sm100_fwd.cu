@@ -1,0 +1,380 @@
+// ssa_sm100_fwd.cu — SSA attention forward for sm_100a: TMA + tcgen05 + TMEM.
+//
+// Computes what the reference's _ssa_attn_fwd computes (ssa_triton_kernel.py:150-260, inner
+// loop :40-124): S = scale * Q K^T, the SSA transform t2 = n * sign(s) * log2(1 + b|s|)
+// (= n * sign(s) * log1p(b|s|) * log2 e, :96-107), an online base-2 normaliser (:110-113),
+// O = P V / l and M = m + log2 l (:248-255).
+//
+// One CTA = one 128-row query tile of one (sequence, q-head). 6 warps:
+//   warp 0      TMEM allocator + TMA producer (Q once, K/V through a 2-stage ring)
+//   warp 1      MMA issuer: S = Q K^T (SS form, fp32 in TMEM), O += P V (TS form: P read
+//               straight from TMEM, where it overwrote S)
+//   warps 2..5  one thread per query row: tcgen05.ld its S row, SSA transform, running max
+//               and sum, P (bf16/f16) written back into TMEM, O correction, epilogue.
+// Two CTAs share an SM (TMEM 2 x 256 columns, ~81 KB shared memory each), so one CTA's
+// transcendental work overlaps the other's tensor-core work.
+//
+// Rescaling: the running max only moves when a block's max exceeds it by more than
+// kRescaleThreshold (log2 units), so P <= 2^8 and O is corrected rarely; m, l and O always
+// refer to the same (possibly stale) max, so the result is exact up to rounding.
+//
+// Every mbarrier wait is bounded (~1 s): on expiry the kernel records SSA_ERR_DEVICE_TIMEOUT in
+// the device status word, unwinds, waits for its own in-flight TMA / MMA work (bounded) and
+// frees its TMEM.
+#include <cudaTypedefs.h>
+
+#include "ssa_internal.h"
+#include "ssa_sm100.cuh"
+#include "ssa_tmap.h"
+
+namespace ssa {
+namespace sm100 {
+
+constexpr float kRescaleThreshold = 8.0f;
+
+template <int D>
+struct FwdCfg {
+  static constexpr int BM = 128;
+  static constexpr int BN = (D == 64) ? 128 : 64;
+  static constexpr int KH = D / 64;  // 64-element (128-byte) column slabs per row
+  static constexpr int STAGES = 2;
+  static constexpr uint32_t Q_BYTES = BM * D * 2;
+  static constexpr uint32_t KV_BYTES = BN * D * 2;
+  static constexpr uint32_t OFF_Q = 0;
+  static constexpr uint32_t OFF_K = Q_BYTES;
+  static constexpr uint32_t OFF_V = OFF_K + STAGES * KV_BYTES;
+  static constexpr uint32_t OFF_BAR = OFF_V + STAGES * KV_BYTES;
+  static constexpr uint32_t SMEM_BYTES = OFF_BAR + 256 + 1024;  // + slack for 1 KB alignment
+  static constexpr uint32_t TMEM_COLS = 256;
+  static constexpr uint32_t COL_S = 0;   // S (fp32, BN columns); P (packed 16-bit) aliases it
+  static constexpr uint32_t COL_O = BN;  // O accumulator (fp32, D columns)
+  static constexpr int THREADS = 192;
+  static_assert(BN + D <= (int)TMEM_COLS, "TMEM budget");
+};
+
+struct FwdArgs {
+  Problem p;
+  TensorRef o;
+  float* lse;
+  unsigned int* status;
+  int tiles_m;
+};
+
+enum FwdBar : int {
+  FB_Q = 0,
+  FB_KF = 1,   // 2 stages
+  FB_VF = 3,   // 2 stages
+  FB_KVE = 5,  // 2 stages
+  FB_S = 7,
+  FB_P = 8,
+  FB_O = 9,
+  FB_END = 10,
+  FB_COUNT = 11
+};
+
+template <int D, bool BF16>
+__global__ void __launch_bounds__(192, 2)
+    fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ,
+                     const __grid_constant__ CUtensorMap tmK,
+                     const __grid_constant__ CUtensorMap tmV, const FwdArgs a) {
+  using C = FwdCfg<D>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t bar0 = sbase + C::OFF_BAR;
+  auto bar = [&](int i) -> uint32_t { return bar0 + 8u * (uint32_t)i; };
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_BAR + 8 * FB_COUNT);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const Problem& p = a.p;
+  const int BH = p.B * p.Hq;
+  const int tile = a.tiles_m - 1 - (int)(blockIdx.x / BH);  // longest causal rows first
+  const int bh = blockIdx.x % BH;
+  const int z = bh / p.Hq, hq = bh % p.Hq, hkv = hq / p.gqa;
+  int seq_start, L;
+  seq_bounds(p, z, seq_start, L);
+  const int m0 = tile * C::BM;
+  // Block-uniform exits, before any barrier or TMEM allocation: nothing to do, or an earlier
+  // launch already recorded a device-side timeout (later launches then cost nothing).
+  if (m0 >= L || *reinterpret_cast<volatile unsigned int*>(a.status) != 0) return;
+  const int kv_len = p.causal ? min(L, m0 + C::BM) : L;
+  const int nblk = (kv_len + C::BN - 1) / C::BN;
+  const int zc = p.cu_seqlens ? 0 : z;
+
+  if (threadIdx.x == 0) {
+    mbar_init(bar(FB_Q), 1);
+    for (int s = 0; s < C::STAGES; ++s) {
+      mbar_init(bar(FB_KF + s), 1);
+      mbar_init(bar(FB_VF + s), 1);
+      mbar_init(bar(FB_KVE + s), 1);
+    }
+    mbar_init(bar(FB_S), 1);
+    mbar_init(bar(FB_P), 128);
+    mbar_init(bar(FB_O), 1);
+    mbar_init(bar(FB_END), 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    __syncwarp();
+    tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producer
+    if (lane == 0) {
+      prefetch_tmap(&tmQ);
+      prefetch_tmap(&tmK);
+      prefetch_tmap(&tmV);
+      mbar_expect_tx(bar(FB_Q), C::Q_BYTES);
+#pragma unroll
+      for (int h = 0; h < C::KH; ++h)
+        tma_load_4d(sbase + C::OFF_Q + h * C::BM * 128, &tmQ, bar(FB_Q), h * 64, seq_start + m0,
+                    hq, zc);
+      int last_use[C::STAGES] = {-1, -1};
+      for (int j = 0; j < nblk; ++j) {
+        const int st = j & 1, u = j >> 1;
+        if (j >= C::STAGES && !mbar_wait(bar(FB_KVE + st), (u - 1) & 1, a.status)) {
+          *abort_flag = 1;
+          break;
+        }
+        if (*abort_flag) break;
+        const int r0 = seq_start + j * C::BN;
+        mbar_expect_tx(bar(FB_KF + st), C::KV_BYTES);
+#pragma unroll
+        for (int h = 0; h < C::KH; ++h)
+          tma_load_4d(sbase + C::OFF_K + st * C::KV_BYTES + h * C::BN * 128, &tmK,
+                      bar(FB_KF + st), h * 64, r0, hkv, zc);
+        mbar_expect_tx(bar(FB_VF + st), C::KV_BYTES);
+#pragma unroll
+        for (int h = 0; h < C::KH; ++h)
+          tma_load_4d(sbase + C::OFF_V + st * C::KV_BYTES + h * C::BN * 128, &tmV,
+                      bar(FB_VF + st), h * 64, r0, hkv, zc);
+        last_use[st] = u;
+      }
+      if (*abort_flag) {  // drain this CTA's own loads before its shared memory is released
+        mbar_wait(bar(FB_Q), 0, a.status);
+        for (int s = 0; s < C::STAGES; ++s)
+          if (last_use[s] >= 0) {
+            mbar_wait(bar(FB_KF + s), last_use[s] & 1, a.status);
+            mbar_wait(bar(FB_VF + s), last_use[s] & 1, a.status);
+          }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc_s = idesc_f16(BF16, false, false, 128, C::BN);
+      constexpr uint32_t idesc_o = idesc_f16(BF16, false, true, 128, D);
+      bool ok = mbar_wait(bar(FB_Q), 0, a.status);
+      for (int j = 0; ok && j < nblk; ++j) {
+        const int st = j & 1, u = j >> 1;
+        ok = mbar_wait(bar(FB_KF + st), u & 1, a.status);
+        // S/P columns are reused: the previous P V must have finished reading P.
+        if (ok && j > 0) ok = mbar_wait(bar(FB_O), (j - 1) & 1, a.status);
+        if (!ok || *abort_flag) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const uint32_t off = (uint32_t)(kk & 3) * 32u;  // 16 elements = 32 B within the slab
+          const uint32_t slab = (uint32_t)(kk >> 2);
+          const uint64_t ad = sdesc_sw128(sbase + C::OFF_Q + slab * C::BM * 128 + off, 16, 1024);
+          const uint64_t bd = sdesc_sw128(
+              sbase + C::OFF_K + st * C::KV_BYTES + slab * C::BN * 128 + off, 16, 1024);
+          mma_ss(tmem + C::COL_S, ad, bd, idesc_s, kk > 0 ? 1u : 0u);
+        }
+        mma_commit(bar(FB_S));
+        ok = mbar_wait(bar(FB_VF + st), u & 1, a.status);
+        if (ok) ok = mbar_wait(bar(FB_P), j & 1, a.status);
+        if (!ok || *abort_flag) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < C::BN / 16; ++kk) {
+          const uint64_t bd = sdesc_sw128(sbase + C::OFF_V + st * C::KV_BYTES + kk * 16 * 128,
+                                          C::BN * 128, 1024);
+          mma_ts(tmem + C::COL_O, tmem + C::COL_S + kk * 8, bd, idesc_o,
+                 (j > 0 || kk > 0) ? 1u : 0u);
+        }
+        mma_commit(bar(FB_O));
+        mma_commit(bar(FB_KVE + st));
+      }
+      if (!ok) *abort_flag = 1;
+      mma_commit(bar(FB_END));  // all MMAs of this CTA retired before TMEM is freed
+      mbar_wait(bar(FB_END), 0, a.status);
+    }
+  } else {
+    // ------------------------------------------------------------------ softmax rows
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;
+    const int row = m0 + r;
+    const uint32_t t_lane = tmem + ((uint32_t)(quad * 32) << 16);
+    const float n = load_n(p, hq);
+    const float cb = __ldg(p.b_ptr) * p.scale;  // b * |scale|; scale > 0 on this path
+    float m_run = -INFINITY, l_run = 0.f;
+    bool ok = true;
+    for (int j = 0; j < nblk; ++j) {
+      ok = mbar_wait(bar(FB_S), j & 1, a.status);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok || *abort_flag) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t sr[C::BN / 32][32];
+#pragma unroll
+      for (int c = 0; c < C::BN / 32; ++c) tmem_ld32(t_lane + C::COL_S + c * 32, sr[c]);
+      tmem_ld_wait_only();
+#pragma unroll
+      for (int c = 0; c < C::BN / 32; ++c) tmem_pin(sr[c]);
+
+      const int n0 = j * C::BN;
+      const bool full = (n0 + C::BN <= L) && (!p.causal || n0 + C::BN - 1 <= m0);
+      float bmax = -INFINITY;
+#pragma unroll
+      for (int c = 0; c < C::BN / 32; ++c) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          const float x = __uint_as_float(sr[c][i]);
+          const float l2 = lg2_approx(fmaf(fabsf(x), cb, 1.0f));
+          float t2 = n * copy_sign_bit(l2, x);
+          if (!full) {
+            const int col = n0 + c * 32 + i;
+            const bool valid = (row < L) && (col < L) && (!p.causal || col <= row);
+            t2 = valid ? t2 : -INFINITY;
+          }
+          sr[c][i] = __float_as_uint(t2);
+          bmax = fmaxf(bmax, t2);
+        }
+      }
+      const float m_new = fmaxf(m_run, bmax);
+      const bool need = m_new > m_run + kRescaleThreshold;
+      float alpha = 1.f;
+      if (need) {
+        alpha = ex2_approx(m_run - m_new);
+        m_run = m_new;
+      }
+      const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
+      float rs = 0.f;
+      uint32_t pk[C::BN / 64][32];
+#pragma unroll
+      for (int c = 0; c < C::BN / 32; ++c) {
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          const float p0 = ex2_approx(__uint_as_float(sr[c][i]) - m_use);
+          const float p1 = ex2_approx(__uint_as_float(sr[c][i + 1]) - m_use);
+          rs += p0 + p1;
+          pk[c >> 1][(c & 1) * 16 + (i >> 1)] = pack2<BF16>(p0, p1);
+        }
+      }
+      l_run = l_run * alpha + rs;
+      // O correction. PV_{j-1} completed before S_j's commit fired (commit tracks every
+      // earlier tcgen05 op of the issuing thread), so O is final for blocks < j here.
+      if (__any_sync(0xffffffffu, need && j > 0)) {
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld32(t_lane + C::COL_O + c * 32, o);
+          tmem_ld_wait(o);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st32(t_lane + C::COL_O + c * 32, o);
+        }
+      }
+#pragma unroll
+      for (int c = 0; c < C::BN / 64; ++c) tmem_st32(t_lane + C::COL_S + c * 32, pk[c]);
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(bar(FB_P));
+    }
+    if (ok) {
+      ok = mbar_wait(bar(FB_O), (nblk - 1) & 1, a.status);
+      ok = __all_sync(0xffffffffu, ok);
+    }
+    if (!ok) {
+      *abort_flag = 1;
+    } else {
+      tc_fence_after();
+      const float l_safe = l_run > 0.f ? l_run : 1.f;
+      const float inv_l = 1.f / l_safe;
+      using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+      T* orow = reinterpret_cast<T*>(a.o.ptr) + row_offset(a.o, p, z, hq, seq_start, row);
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t o[32];
+        tmem_ld32(t_lane + C::COL_O + c * 32, o);
+        tmem_ld_wait(o);
+        if (row < L) {
+          uint32_t w[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            w[i] = pack2<BF16>(__uint_as_float(o[2 * i]) * inv_l,
+                               __uint_as_float(o[2 * i + 1]) * inv_l);
+          uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            dst[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+        }
+      }
+      if (row < L) a.lse[stat_offset(p, z, hq, seq_start, row)] = m_run + log2f(l_safe);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+template <int D, bool BF16>
+int run_fwd(const Problem& p, TensorRef q, TensorRef k, TensorRef v, TensorRef o, float* lse,
+            cudaStream_t st) {
+  using C = FwdCfg<D>;
+  const int dtype = BF16 ? SSA_DTYPE_BF16 : SSA_DTYPE_F16;
+  CUtensorMap tq, tk, tv;
+  int rc;
+  if ((rc = make_tmap_bhnd(&tq, q, p, dtype, p.Hq, C::BM)) != SSA_OK) return rc;
+  if ((rc = make_tmap_bhnd(&tk, k, p, dtype, p.Hkv, C::BN)) != SSA_OK) return rc;
+  if ((rc = make_tmap_bhnd(&tv, v, p, dtype, p.Hkv, C::BN)) != SSA_OK) return rc;
+  FwdArgs a;
+  a.p = p;
+  a.o = o;
+  a.lse = lse;
+  a.status = device_status_ptr();
+  a.tiles_m = (p.max_seqlen + C::BM - 1) / C::BM;
+  auto kern = fwd_sm100_kernel<D, BF16>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)C::SMEM_BYTES) != cudaSuccess)
+    return SSA_ERR_CUDA;
+  const long long grid = (long long)a.tiles_m * p.B * p.Hq;
+  kern<<<(unsigned)grid, C::THREADS, C::SMEM_BYTES, st>>>(tq, tk, tv, a);
+  note_launches(1);
+  return SSA_OK;
+}
+
+}  // namespace sm100
+
+bool sm100_supports(int dtype, int D) {
+  return (dtype == SSA_DTYPE_BF16 || dtype == SSA_DTYPE_F16) && (D == 64 || D == 128);
+}
+
+int launch_fwd_sm100(int dtype, const Problem& p, TensorRef q, TensorRef k, TensorRef v,
+                     TensorRef o, float* lse, cudaStream_t st) {
+  const bool bf = dtype == SSA_DTYPE_BF16;
+  if (p.D == 64) return bf ? sm100::run_fwd<64, true>(p, q, k, v, o, lse, st)
+                           : sm100::run_fwd<64, false>(p, q, k, v, o, lse, st);
+  if (p.D == 128) return bf ? sm100::run_fwd<128, true>(p, q, k, v, o, lse, st)
+                            : sm100::run_fwd<128, false>(p, q, k, v, o, lse, st);
+  return SSA_ERR_UNSUPPORTED;
+}
+
+}  // namespace ssa

@@ -1,0 +1,134 @@
+"""C-ABI library checks that need no GPU: it loads, exports every function include/ssa_b200.h
+declares, sizes workspaces, rejects bad problems with the right status codes, and the Python
+host layer (module shims, parameters, checkpoint keys) behaves like the reference's."""
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+import torch
+
+REPO = Path(__file__).resolve().parent.parent
+
+
+@pytest.fixture(scope="module")
+def lib():
+    from SSA import _lib
+    if not _lib.LIB_PATH.exists():
+        import __graft_entry__
+        __graft_entry__.build()
+    return _lib.load()
+
+
+def header_functions():
+    text = (REPO / "include" / "ssa_b200.h").read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?\w+\s*\*?\s*(ssa_\w+)\s*\(", text, flags=re.M)))
+
+
+def test_header_declares_expected_entry_points():
+    fns = header_functions()
+    for f in ("ssa_attn_fwd", "ssa_attn_bwd", "ssa_attn_bwd_preprocess",
+              "ssa_attn_bwd_workspace_size", "ssa_attn_fwd_workspace_size",
+              "ssa_attn_kernel_family", "ssa_device_status", "ssa_last_error", "ssa_version"):
+        assert f in fns
+
+
+def test_library_exports_every_declared_symbol(lib):
+    for f in header_functions():
+        assert hasattr(lib, f), f"libssa_b200.so does not export {f}"
+    from SSA import _lib
+    assert set(_lib.EXPORTED_SYMBOLS) <= set(header_functions())
+
+
+def test_version(lib):
+    assert b"sm_100a" in lib.ssa_version()
+
+
+def _prob(**kw):
+    from SSA import _lib
+    base = dict(dtype=2, B=2, Hq=8, Hkv=2, N=256, D=64, causal=1, softmax_scale=0.125,
+                ssa_n=1, n_per_head=0, ssa_b=1, cu_seqlens=None, max_seqlen=0)
+    base.update(kw)
+    return _lib.SsaProblem(**base)
+
+
+def test_family_selection(lib):
+    assert lib.ssa_attn_kernel_family(ctypes.byref(_prob())) == 1          # bf16 D=64
+    assert lib.ssa_attn_kernel_family(ctypes.byref(_prob(dtype=1, D=128))) == 1
+    assert lib.ssa_attn_kernel_family(ctypes.byref(_prob(dtype=0))) == 0   # fp32 -> generic
+    assert lib.ssa_attn_kernel_family(ctypes.byref(_prob(D=32))) == 0      # D=32 -> generic
+    assert lib.ssa_attn_kernel_family(ctypes.byref(_prob(softmax_scale=-1.0))) == 0
+    assert lib.ssa_attn_kernel_family(ctypes.byref(_prob(Hq=6, Hkv=4))) == -1
+
+
+def test_bad_problems_rejected_before_any_cuda_call(lib):
+    from SSA import _lib
+    t = _lib.SsaTensor(16, 0, 0, 0)
+    cases = [(_prob(Hq=6, Hkv=4), _lib.SSA_ERR_BAD_SHAPE, b"divisible"),
+             (_prob(D=48), _lib.SSA_ERR_UNSUPPORTED, b"head dim"),
+             (_prob(dtype=7), _lib.SSA_ERR_UNSUPPORTED, b"dtype"),
+             (_prob(N=0), _lib.SSA_ERR_BAD_SHAPE, b"non-positive"),
+             (_prob(ssa_n=None), _lib.SSA_ERR_NULL, b"ssa_n"),
+             (_prob(cu_seqlens=64, max_seqlen=0), _lib.SSA_ERR_BAD_SHAPE, b"max_seqlen")]
+    for prob, code, msg in cases:
+        rc = lib.ssa_attn_fwd(ctypes.byref(prob), t, t, t, t, 16, None, 0, None)
+        assert rc == code, (rc, code)
+        assert msg in lib.ssa_last_error()
+    rc = lib.ssa_attn_fwd(ctypes.byref(_prob()), _lib.SsaTensor(None, 0, 0, 0), t, t, t, 16,
+                          None, 0, None)
+    assert rc == _lib.SSA_ERR_NULL and b"q is NULL" in lib.ssa_last_error()
+
+
+def test_bwd_workspace_requirement_enforced(lib):
+    from SSA import _lib
+    prob = _prob()
+    need = lib.ssa_attn_bwd_workspace_size(ctypes.byref(prob))
+    # delta alone is Hq * B * N fp32
+    assert need >= 8 * 2 * 256 * 4
+    t = _lib.SsaTensor(16, 0, 0, 0)
+    rc = lib.ssa_attn_bwd(ctypes.byref(prob), t, t, t, t, t, 16, t, t, t, 16, 16, 16, need - 1, None)
+    assert rc == _lib.SSA_ERR_WORKSPACE
+    # fp32 generic workspace also holds the dn/db partials
+    p32 = _prob(dtype=0)
+    assert lib.ssa_attn_bwd_workspace_size(ctypes.byref(p32)) >= need
+
+
+def test_python_layer_rejects_cpu_tensors():
+    from SSA.ssa_flash_attention import ssa_flash_attention
+    q = torch.randn(1, 2, 8, 16)
+    with pytest.raises(ValueError, match="CUDA"):
+        ssa_flash_attention(q, q, q, 0.25, torch.tensor(1.5), torch.tensor(0.8))
+
+
+def test_module_matches_reference_construction():
+    from SSA.ssa_triton_attention import SSAAttentionConfig, SSATritonAttention
+    cfg = SSAAttentionConfig(num_attention_heads=32, kv_channels=64, num_query_groups=8,
+                             apply_query_key_layer_scaling=True)
+    m = SSATritonAttention(cfg, layer_number=4, ssa_n=1.5, ssa_b=0.8)
+    assert m.gqa_ratio == 4
+    assert abs(m.softmax_scale - 1.0 / 8.0 / 4) < 1e-12
+    keys = set(m.state_dict().keys())
+    assert keys == {"ssa_n_raw", "ssa_b"}          # checkpoint keys of the reference
+    assert m.ssa_n_raw.requires_grad and m.ssa_n_raw.dim() == 0
+    m2 = SSATritonAttention(cfg, 1, learnable_ssa=True, learnable_b=True)
+    assert set(m2.state_dict().keys()) == {"ssa_n_raw", "ssa_b_raw"}
+    m3 = SSATritonAttention(cfg, 1, learnable_ssa=False)
+    assert set(m3.state_dict().keys()) == {"ssa_n", "ssa_b"}
+    m4 = SSATritonAttention(cfg, 1, ssa_n=[0.43] * 32)
+    assert m4.ssa_n_raw.shape == (32,)
+    with pytest.raises(AssertionError):
+        SSATritonAttention(SSAAttentionConfig(32, 64, 8, context_parallel_size=2), 1)
+
+
+def test_layer_spec_requires_megatron_only_when_called():
+    import SSA.ssa_triton_layer_specs as ls
+    f = ls.get_bias_dropout_add(False, False)
+    x = torch.ones(3)
+    assert torch.equal(f((x, None), x, 0.0), 2 * x)
+    try:
+        import megatron  # noqa: F401
+    except ImportError:
+        with pytest.raises(ImportError):
+            ls.get_ssa_triton_gpt_layer_spec()

@@ -1,0 +1,283 @@
+"""GPU parity: the CUDA kernels (through libssa_b200.so's C ABI) against the CPU oracle and the
+reference's golden vectors, on identical seeded inputs.
+
+Tolerances (written here, applied below):
+  * fp32 inputs (generic kernels): max|a-r| / max|r| <= 1e-5 for out/dq/dk/dv, and
+    |a-r| <= 1e-5 * |r| + 1e-6 for dn/db.
+  * bf16/fp16 inputs (tcgen05 kernels for D in {64,128}): against the fp64 oracle evaluated on
+    the same 16-bit inputs, elementwise |a-r| <= 2e-2 + 5e-2 |r| (the reference's own bf16 rule,
+    check_ssa_triton_parity.py:1059-1062) AND max-abs <= 2e-2 wherever |r| <= 1 (bf16 cannot
+    represent values above 4 to within 2e-2 absolute: its spacing there is 2^-5);
+    dn/db: |a-r| <= 2e-3 + 2e-2 |r| (check_ssa_triton_parity.py:1066-1067).
+"""
+
+import math
+
+import pytest
+import torch
+
+from conftest import golden_qkv, load_golden
+from oracle.ssa_oracle import max_rel, ssa_reference_grads, ssa_reference_grads_varlen
+
+pytestmark = pytest.mark.gpu
+
+GOLDEN = load_golden()
+
+
+def _api():
+    from SSA import ssa_triton_kernel as K
+    return K
+
+
+def assert_lowp_close(name, got, ref):
+    g = got.detach().double().cpu()
+    r = ref.detach().double().cpu()
+    assert g.shape == r.shape, name
+    assert torch.isfinite(g).all(), f"{name}: non-finite"
+    d = (g - r).abs()
+    lim = 2e-2 + 5e-2 * r.abs()
+    bad = int((d > lim).sum())
+    assert bad == 0, f"{name}: {bad} elements outside 2e-2+5e-2|r| (max|d|={d.max():.3e})"
+    small = r.abs() <= 1.0
+    if small.any():
+        assert d[small].max() <= 2e-2, f"{name}: max-abs {d[small].max():.3e} > 2e-2 on |r|<=1"
+
+
+def assert_scalar_close(name, got, ref, atol=2e-3, rtol=2e-2):
+    g = torch.as_tensor(got).double().cpu().reshape(-1)
+    r = torch.as_tensor(ref).double().cpu().reshape(-1)
+    assert g.shape == r.shape, name
+    d = (g - r).abs()
+    assert (d <= atol + rtol * r.abs()).all(), f"{name}: {g.tolist()} vs {r.tolist()}"
+
+
+def run_fwd_bwd(q, k, v, do, scale, n, b, causal):
+    K = _api()
+    out, m = K.ssa_flash_attn_forward(q, k, v, scale, n, b, causal=causal)
+    dq, dk, dv, dn, db = K.ssa_flash_attn_backward(q, k, v, out, do, m, scale, n, b, causal=causal)
+    torch.cuda.synchronize()
+    return dict(out=out, m=m, dq=dq, dk=dk, dv=dv, dn=dn, db=db)
+
+
+def seeded(shape, seed, scale=1.0, dtype=torch.bfloat16):
+    g = torch.Generator().manual_seed(seed)
+    return (torch.randn(*shape, generator=g) * scale).to(dtype)
+
+
+# ----------------------------------------------------------------------------- golden vectors
+@pytest.mark.parametrize("meta,arrays", GOLDEN, ids=[m["name"] for m, _ in GOLDEN])
+def test_golden_fp32(meta, arrays, cuda_device):
+    q, k, v, do = golden_qkv(meta, arrays, device=cuda_device)
+    n = torch.tensor(meta["ssa_n"], device=cuda_device)
+    b = torch.tensor(meta["ssa_b"], device=cuda_device)
+    r = run_fwd_bwd(q, k, v, do, meta["softmax_scale"], n, b, meta["causal"])
+    for name in ("out", "dq", "dk", "dv"):
+        err = max_rel(r[name].cpu(), torch.from_numpy(arrays[name]))
+        assert err <= 1e-5, f"{name}: max-rel {err:.3e}"
+    assert (r["m"].cpu().double() - torch.from_numpy(arrays["m"]).double()).abs().max() < 1e-5
+    for name in ("dn", "db"):
+        ref = float(arrays[name])
+        assert abs(float(r[name]) - ref) <= 1e-5 * abs(ref) + 1e-6, (name, float(r[name]), ref)
+
+
+@pytest.mark.parametrize("meta,arrays", GOLDEN, ids=[m["name"] for m, _ in GOLDEN])
+def test_golden_bf16(meta, arrays, cuda_device):
+    """bf16 inputs against the fp64 oracle on the same bf16 values; for the case whose inputs
+    are bf16-representable the reference's fp32 golden outputs are checked directly too."""
+    q, k, v, do = golden_qkv(meta, arrays, device=cuda_device, dtype=torch.bfloat16)
+    n = torch.tensor(meta["ssa_n"], device=cuda_device)
+    b = torch.tensor(meta["ssa_b"], device=cuda_device)
+    r = run_fwd_bwd(q, k, v, do, meta["softmax_scale"], n, b, meta["causal"])
+    ref = ssa_reference_grads(q.cpu(), k.cpu(), v.cpu(), meta["softmax_scale"], n.cpu(), b.cpu(),
+                              do.cpu(), meta["causal"])
+    for name in ("out", "dq", "dk", "dv"):
+        assert_lowp_close(name, r[name], ref[name])
+    assert_scalar_close("dn", r["dn"], ref["dn"])
+    assert_scalar_close("db", r["db"], ref["db"])
+    if meta["bf16_representable"]:
+        for name in ("out", "dq", "dk", "dv"):
+            assert_lowp_close(name + "(golden)", r[name], torch.from_numpy(arrays[name]))
+        assert_scalar_close("dn(golden)", r["dn"], float(arrays["dn"]))
+
+
+# ----------------------------------------------------------------------------- tensor-core path
+CASES = [
+    # B, Hq, Hkv, N, D, causal, dtype, per_head_n
+    (2, 8, 2, 512, 64, True, torch.bfloat16, False),
+    (1, 4, 4, 512, 64, False, torch.bfloat16, False),
+    (1, 8, 2, 384, 64, True, torch.bfloat16, True),
+    (2, 4, 1, 200, 64, True, torch.bfloat16, False),    # ragged: N not a tile multiple
+    (1, 4, 1, 333, 64, False, torch.bfloat16, True),
+    (1, 4, 2, 256, 128, True, torch.bfloat16, False),
+    (1, 2, 1, 300, 128, False, torch.bfloat16, False),
+    (1, 8, 2, 256, 64, True, torch.float16, True),
+    (1, 4, 4, 130, 128, True, torch.float16, False),
+    (1, 4, 2, 64, 64, True, torch.bfloat16, False),     # shorter than one tile
+]
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,N,D,causal,dtype,per_head", CASES)
+def test_kernel_vs_oracle(B, Hq, Hkv, N, D, causal, dtype, per_head, cuda_device):
+    K = _api()
+    seed = B * 1000 + Hq * 100 + N + D
+    q = seeded((B, Hq, N, D), seed, 0.5, dtype)
+    k = seeded((B, Hkv, N, D), seed + 1, 0.5, dtype)
+    v = seeded((B, Hkv, N, D), seed + 2, 0.5, dtype)
+    do = seeded((B, Hq, N, D), seed + 3, 1.0, dtype)
+    if per_head:
+        n = 0.3 + 0.3 * torch.rand(Hq, generator=torch.Generator().manual_seed(seed + 4))
+    else:
+        n = torch.tensor(0.43)
+    b = torch.tensor(0.8)
+    scale = 1.0 / math.sqrt(D)
+    assert K.kernel_family(q.to(cuda_device), scale) == 1
+    r = run_fwd_bwd(q.to(cuda_device), k.to(cuda_device), v.to(cuda_device), do.to(cuda_device),
+                    scale, n.to(cuda_device), b.to(cuda_device), causal)
+    ref = ssa_reference_grads(q, k, v, scale, n, b, do, causal)
+    for name in ("out", "dq", "dk", "dv"):
+        assert_lowp_close(name, r[name], ref[name])
+    assert (r["m"].cpu().double() - ref["lse2"]).abs().max() < 2e-3
+    assert r["dn"].shape == n.shape
+    assert_scalar_close("dn", r["dn"], ref["dn"])
+    assert_scalar_close("db", r["db"], ref["db"])
+
+
+def test_strided_megatron_layout(cuda_device):
+    """[S, B, H, D]-permuted views (check_ssa_triton_parity.py:262-265) go through TMA as-is."""
+    K = _api()
+    S, B, Hq, Hkv, D = 256, 2, 8, 2, 64
+    qs = seeded((S, B, Hq, D), 11, 0.5).to(cuda_device)
+    ks = seeded((S, B, Hkv, D), 12, 0.5).to(cuda_device)
+    vs = seeded((S, B, Hkv, D), 13, 0.5).to(cuda_device)
+    q, k, v = (t.permute(1, 2, 0, 3) for t in (qs, ks, vs))
+    do = seeded((B, Hq, S, D), 14).to(cuda_device)
+    n, b = torch.tensor(1.5, device=cuda_device), torch.tensor(0.8, device=cuda_device)
+    r = run_fwd_bwd(q, k, v, do, D ** -0.5, n, b, True)
+    assert r["out"].stride() == q.stride()  # empty_like keeps the Megatron layout
+    ref = ssa_reference_grads(q.cpu(), k.cpu(), v.cpu(), D ** -0.5, n.cpu(), b.cpu(), do.cpu(), True)
+    for name in ("out", "dq", "dk", "dv"):
+        assert_lowp_close(name, r[name], ref[name])
+    assert_scalar_close("dn", r["dn"], ref["dn"])
+
+
+def test_fp32_generic_path(cuda_device):
+    """fp32 within 1e-5 relative (BASELINE config 1 shape, reduced batch*heads)."""
+    q = seeded((1, 4, 512, 64), 21, 1.0, torch.float32)
+    k = seeded((1, 4, 512, 64), 22, 1.0, torch.float32)
+    v = seeded((1, 4, 512, 64), 23, 1.0, torch.float32)
+    do = seeded((1, 4, 512, 64), 24, 1.0, torch.float32)
+    n = torch.full((4,), 0.43)
+    b = torch.tensor(0.8)
+    r = run_fwd_bwd(q.to(cuda_device), k.to(cuda_device), v.to(cuda_device), do.to(cuda_device),
+                    0.125, n.to(cuda_device), b.to(cuda_device), True)
+    ref = ssa_reference_grads(q, k, v, 0.125, n, b, do, True)
+    for name in ("out", "dq", "dk", "dv"):
+        assert max_rel(r[name].cpu(), ref[name]) <= 1e-5, name
+    assert torch.allclose(r["dn"].cpu().double(), ref["dn"], rtol=1e-5, atol=1e-6)
+    assert abs(float(r["db"]) - float(ref["db"])) <= 1e-5 * abs(float(ref["db"])) + 1e-6
+
+
+@pytest.mark.parametrize("D,dtype", [(64, torch.bfloat16), (128, torch.bfloat16),
+                                     (32, torch.bfloat16), (64, torch.float32)])
+def test_varlen_packed_documents(D, dtype, cuda_device):
+    K = _api()
+    lens = [100, 257, 31, 512, 128]
+    T = sum(lens)
+    cu = torch.tensor([0] + list(torch.tensor(lens).cumsum(0)), dtype=torch.int32)
+    Hq, Hkv = 8, 2
+    q = seeded((T, Hq, D), 31, 0.5, dtype)
+    k = seeded((T, Hkv, D), 32, 0.5, dtype)
+    v = seeded((T, Hkv, D), 33, 0.5, dtype)
+    do = seeded((T, Hq, D), 34, 1.0, dtype)
+    n, b = torch.tensor(0.43), torch.tensor(0.8)
+    dev = cuda_device
+    out, lse = K.ssa_flash_attn_varlen_forward(q.to(dev), k.to(dev), v.to(dev), cu.to(dev),
+                                               max(lens), D ** -0.5, n.to(dev), b.to(dev), True)
+    dq, dk, dv, dn, db = K.ssa_flash_attn_varlen_backward(
+        q.to(dev), k.to(dev), v.to(dev), out, do.to(dev), lse, cu.to(dev), max(lens), D ** -0.5,
+        n.to(dev), b.to(dev), True)
+    torch.cuda.synchronize()
+    ref = ssa_reference_grads_varlen(q, k, v, cu, D ** -0.5, n, b, do, True)
+    got = dict(out=out, dq=dq, dk=dk, dv=dv)
+    for name in ("out", "dq", "dk", "dv"):
+        if dtype == torch.float32:
+            assert max_rel(got[name].cpu(), ref[name]) <= 1e-5, name
+        else:
+            assert_lowp_close(name, got[name], ref[name])
+    assert (lse.cpu().double() - ref["lse2"].transpose(0, 1)).abs().max() < 2e-3
+    assert_scalar_close("dn", dn, ref["dn"])
+    assert_scalar_close("db", db, ref["db"])
+
+
+def test_bit_deterministic(cuda_device):
+    """Two identical runs are bit-identical (check_ssa_triton_parity.py:507-562, atol 0)."""
+    q = seeded((2, 8, 384, 64), 41, 0.5).to(cuda_device)
+    k = seeded((2, 2, 384, 64), 42, 0.5).to(cuda_device)
+    v = seeded((2, 2, 384, 64), 43, 0.5).to(cuda_device)
+    do = seeded((2, 8, 384, 64), 44).to(cuda_device)
+    n, b = torch.tensor(1.5, device=cuda_device), torch.tensor(0.8, device=cuda_device)
+    r1 = run_fwd_bwd(q, k, v, do, 0.125, n, b, True)
+    r2 = run_fwd_bwd(q, k, v, do, 0.125, n, b, True)
+    for name in r1:
+        assert torch.equal(r1[name], r2[name]), name
+
+
+def test_autograd_function_and_module(cuda_device):
+    from SSA.ssa_flash_attention import ssa_flash_attention
+    from SSA.ssa_triton_attention import SSAAttentionConfig, SSATritonAttention
+    S, B, Hq, Hkv, D = 256, 2, 8, 2, 64
+    cfg = SSAAttentionConfig(num_attention_heads=Hq, kv_channels=D, num_query_groups=Hkv)
+    mod = SSATritonAttention(cfg, layer_number=1, ssa_n=1.5, ssa_b=0.8).to(cuda_device)
+    qs = seeded((S, B, Hq, D), 51, 0.5).to(cuda_device).requires_grad_(True)
+    ks = seeded((S, B, Hkv, D), 52, 0.5).to(cuda_device).requires_grad_(True)
+    vs = seeded((S, B, Hkv, D), 53, 0.5).to(cuda_device).requires_grad_(True)
+    ctx = mod(qs, ks, vs, None)
+    assert ctx.shape == (S, B, Hq * D)
+    g = seeded((S, B, Hq * D), 54).to(cuda_device)
+    ctx.backward(g)
+    q, k, v = (t.detach().cpu().permute(1, 2, 0, 3) for t in (qs, ks, vs))
+    do = g.cpu().reshape(S, B, Hq, D).permute(1, 2, 0, 3)
+    ref = ssa_reference_grads(q, k, v, D ** -0.5, torch.tensor(1.5), torch.tensor(0.8), do, True)
+    assert_lowp_close("ctx", ctx.detach().reshape(S, B, Hq, D).permute(1, 2, 0, 3), ref["out"])
+    assert_lowp_close("dq", qs.grad.permute(1, 2, 0, 3), ref["dq"])
+    assert_lowp_close("dk", ks.grad.permute(1, 2, 0, 3), ref["dk"])
+    assert_scalar_close("dn", mod.ssa_n_raw.grad, ref["dn"])
+    # autograd.Function returns 9 grads, dn shaped like ssa_n, db computed even if unused
+    n = torch.full((Hq,), 0.5, device=cuda_device, requires_grad=True)
+    b = torch.tensor(0.8, device=cuda_device, requires_grad=True)
+    qd = q.to(cuda_device).requires_grad_(True)
+    out = ssa_flash_attention(qd, k.to(cuda_device), v.to(cuda_device), D ** -0.5, n, b, True)
+    out.sum().backward()
+    assert n.grad.shape == (Hq,) and b.grad.shape == ()
+
+
+def test_config2_full_size_slice(cuda_device):
+    """BASELINE config 2 shape (B=8, Hq=32, Hkv=8, S=2048, D=64, bf16, causal, per-head n). The
+    (batch, kv-group) units are independent, so one unit's 4 q-heads are checked exactly against
+    the fp64 oracle at full sequence length."""
+    B, Hq, Hkv, N, D = 8, 32, 8, 2048, 64
+    gen = torch.Generator(device="cpu").manual_seed(0)
+    q = (torch.randn(B, Hq, N, D, generator=gen) * 0.5).to(torch.bfloat16)
+    k = (torch.randn(B, Hkv, N, D, generator=gen) * 0.5).to(torch.bfloat16)
+    v = (torch.randn(B, Hkv, N, D, generator=gen) * 0.5).to(torch.bfloat16)
+    do = torch.randn(B, Hq, N, D, generator=gen).to(torch.bfloat16)
+    n = 0.3 + 0.3 * torch.rand(Hq, generator=gen)
+    b = torch.tensor(0.8)
+    dev = cuda_device
+    r = run_fwd_bwd(q.to(dev), k.to(dev), v.to(dev), do.to(dev), D ** -0.5, n.to(dev), b.to(dev), True)
+    zb, g0 = 3, 5  # batch 3, kv head 5 -> q heads 20..23
+    hs = slice(4 * g0, 4 * g0 + 4)
+    ref = ssa_reference_grads(q[zb:zb + 1, hs], k[zb:zb + 1, g0:g0 + 1], v[zb:zb + 1, g0:g0 + 1],
+                              D ** -0.5, n[hs], b, do[zb:zb + 1, hs], True)
+    assert_lowp_close("out", r["out"][zb:zb + 1, hs], ref["out"])
+    assert_lowp_close("dq", r["dq"][zb:zb + 1, hs], ref["dq"])
+    assert_lowp_close("dk", r["dk"][zb:zb + 1, g0:g0 + 1], ref["dk"])
+    assert_lowp_close("dv", r["dv"][zb:zb + 1, g0:g0 + 1], ref["dv"])
+    for t in r.values():
+        assert torch.isfinite(t).all()
+
+
+def test_device_status_clean(cuda_device):
+    from SSA import _lib
+    rc = _lib.load().ssa_device_status(_lib.stream_ptr(cuda_device))
+    assert rc == _lib.SSA_OK

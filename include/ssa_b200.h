@@ -89,6 +89,20 @@ int ssa_attn_bwd(const ssa_problem_t* prob,
                  void* workspace, size_t workspace_bytes, void* stream);
 size_t ssa_attn_bwd_workspace_size(const ssa_problem_t* prob);
 
+/* Backward that allocates nothing and takes no workspace. No counterpart in the reference.
+ * For callers that cannot allocate device memory where they run the backward (a binding from
+ * another host language with no device allocator, or a loop whose device memory is reserved
+ * up front by another allocator). Runs the generic CUDA-core backward kernels with their
+ * scratch (delta and dn/db partials) in a fixed 16 MiB device array owned by the library:
+ * problems needing more return SSA_ERR_WORKSPACE; calls that overlap on one GPU race on the
+ * array; the first call on each device resolves the array's address (make it before any stream
+ * capture starts). Results match ssa_attn_bwd within the library's parity tolerances. */
+int ssa_attn_bwd_noalloc(const ssa_problem_t* prob,
+                         ssa_tensor_t q, ssa_tensor_t k, ssa_tensor_t v,
+                         ssa_tensor_t out, ssa_tensor_t dout, const float* lse,
+                         ssa_tensor_t dq, ssa_tensor_t dk, ssa_tensor_t dv,
+                         float* dn, float* db, void* stream);
+
 /* Which kernel family serves this problem: 0 = generic (fp32-compute SIMT: fp32 inputs or
  * head dims without a tensor-core kernel), 1 = sm_100a tcgen05/TMA kernels. */
 int ssa_attn_kernel_family(const ssa_problem_t* prob);

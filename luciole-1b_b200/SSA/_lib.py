@@ -31,7 +31,7 @@ DTYPE_CODES = {torch.float32: 0, torch.float16: 1, torch.bfloat16: 2}
 EXPORTED_SYMBOLS = (
     "ssa_attn_fwd", "ssa_attn_fwd_workspace_size", "ssa_attn_bwd_preprocess", "ssa_attn_bwd",
     "ssa_attn_bwd_workspace_size", "ssa_attn_kernel_family", "ssa_device_status",
-    "ssa_last_error", "ssa_version", "ssa_kernel_launch_count",
+    "ssa_last_error", "ssa_version", "ssa_kernel_launch_count", "ssa_attn_bwd_noalloc",
 )
 
 
@@ -85,6 +85,8 @@ def load() -> ctypes.CDLL:
         lib.ssa_attn_bwd_preprocess.restype = ctypes.c_int
         lib.ssa_attn_bwd.argtypes = [P, T, T, T, T, T, vp, T, T, T, vp, vp, vp, sz, vp]
         lib.ssa_attn_bwd.restype = ctypes.c_int
+        lib.ssa_attn_bwd_noalloc.argtypes = [P, T, T, T, T, T, vp, T, T, T, vp, vp, vp]
+        lib.ssa_attn_bwd_noalloc.restype = ctypes.c_int
         lib.ssa_attn_bwd_workspace_size.argtypes = [P]
         lib.ssa_attn_bwd_workspace_size.restype = sz
         lib.ssa_attn_kernel_family.argtypes = [P]

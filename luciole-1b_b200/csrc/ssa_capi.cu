@@ -175,6 +175,19 @@ std::atomic<uint64_t> g_launches{0};
 }
 void note_launches(int n) { g_launches.fetch_add((uint64_t)n, std::memory_order_relaxed); }
 
+int abi_validate_problem(const ssa_problem_t* pr) {
+  g_err[0] = 0;
+  return check_problem(pr);
+}
+Problem abi_to_problem(const ssa_problem_t* pr) { return to_problem(pr); }
+int abi_error(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
 }  // namespace ssa
 
 using namespace ssa;

@@ -36,4 +36,11 @@ unsigned int* device_status_ptr();
 // Host-side count of kernel launches issued by this library (ssa_kernel_launch_count).
 void note_launches(int n);
 
+// Shared C-ABI helpers (ssa_capi.cu): problem validation (status code, message set on
+// failure), conversion to the device-side Problem, and recording an error message that
+// ssa_last_error() then returns.
+int abi_validate_problem(const ssa_problem_t* pr);
+Problem abi_to_problem(const ssa_problem_t* pr);
+int abi_error(int code, const char* fmt, ...);
+
 }  // namespace ssa

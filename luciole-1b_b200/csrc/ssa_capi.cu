@@ -283,7 +283,9 @@ int ssa_attn_bwd(const ssa_problem_t* prob, ssa_tensor_t q, ssa_tensor_t k, ssa_
   if ((rc = finish_launch(rc, "ssa_attn_bwd(preprocess)")) != SSA_OK) return rc;
   if (use_sm100_bwd(prob)) {
     if ((rc = check_tma(p, q, p.Hq, "q")) || (rc = check_tma(p, k, p.Hkv, "k")) ||
-        (rc = check_tma(p, v, p.Hkv, "v")) || (rc = check_tma(p, dout, p.Hq, "dout")))
+        (rc = check_tma(p, v, p.Hkv, "v")) || (rc = check_tma(p, dout, p.Hq, "dout")) ||
+        (rc = check_tma(p, dq, p.Hq, "dq")) || (rc = check_tma(p, dk, p.Hkv, "dk")) ||
+        (rc = check_tma(p, dv, p.Hkv, "dv")))
       return rc;
     if (!device_status_ptr()) return fail(SSA_ERR_CUDA, "cannot resolve the device status word");
     return finish_launch(launch_bwd_sm100(prob->dtype, p, to_ref(q), to_ref(k), to_ref(v),

@@ -1,24 +1,589 @@
-// ssa_sm100_bwd.cu — SSA attention backward for sm_100a (tcgen05/TMA); not yet enabled.
+// ssa_sm100_bwd.cu — SSA attention backward for sm_100a: one fused tcgen05/TMA kernel.
+//
+// Computes what the reference's _ssa_attn_bwd computes (ssa_triton_kernel.py:488-719, inner
+// loops :305-401 and :408-481) in a single pass: for each score element the SSA transform and
+// P = exp2(t2 - M) are recomputed ONCE (the reference recomputes them twice, once for dK/dV and
+// once for dQ), and
+//     dV += P^T dO,   dP = dO V^T,   ds_ssa = P (dP - delta),
+//     dS  = ds_ssa * n b / (1 + b|s|) * scale,   dK += dS^T Q,   dQ += dS K,
+//     dn += ds_ssa * sign(s) log1p(b|s|),   db += ds_ssa * n s / (1 + b|s|)    (:372-397).
+//
+// One CTA owns a 128-row key block of one (sequence, kv-head) and walks every q-head of its GQA
+// group (ssa_triton_kernel.py:573) and every 128-row query tile that can see the block. Per query
+// tile, the two 64-row halves are handled by two warp-groups in ping-pong:
+//   warp 0      TMA producer: K, V once; Q and dO tiles through a 2-stage ring; the tile's
+//               lse / delta rows into shared memory with plain loads.
+//   warp 1      MMA issuer (tcgen05, fp32 accumulation in TMEM):
+//                 S^T  = K Q_h^T,  dP^T = V dO_h^T          (SS, M=128 keys, N=64 queries)
+//                 dV  += P^T dO_h,  dK += dS^T Q_h          (TS: P^T / dS^T read from TMEM)
+//                 dQ   = dS K                               (SS, M=128 queries, dS from smem)
+//   warps 2..5  half 0 of each tile, one thread per key row: SSA transform, P, dS, dn/db
+//   warps 6..9  half 1 of each tile
+//   warps 10..13 dQ drain: TMEM -> shared staging -> one TMA bulk reduce-add (fp32) into the
+//               dQ accumulator in global memory; a small kernel converts it to dq's dtype.
+// TMEM (512 columns): S/dP for half 0 [0,128), for half 1 [128,256), dK [256,320),
+// dV [320,384), dQ [384,448). P^T and dS^T (packed 16-bit) overwrite the S and dP columns
+// they were computed from.
+//
+// dn / db: per-thread fp32 sums, reduced per warp at the end of each q-head and written as
+// partials [z][hq][key block][half][warp]; a deterministic fp64 kernel sums them.
+// dQ accumulation order across key blocks is not fixed (L2 reduce-adds), so dq may differ in
+// the last bits from run to run; dk, dv, dn, db are bit-deterministic.
+//
+// Every mbarrier wait is bounded (~1 s); on expiry the kernel records SSA_ERR_DEVICE_TIMEOUT in
+// the device status word and unwinds (later launches then skip their work).
+#include <cudaTypedefs.h>
+
 #include "ssa_internal.h"
+#include "ssa_sm100.cuh"
+#include "ssa_tmap.h"
 
 namespace ssa {
+namespace sm100 {
+
+struct BwdCfg {
+  static constexpr int D = 64;
+  static constexpr int BN = 128;  // key rows per CTA
+  static constexpr int BT = 128;  // query rows per tile (two 64-row halves)
+  static constexpr uint32_t KV_BYTES = BN * D * 2;   // 16 KB
+  static constexpr uint32_t QT_BYTES = BT * D * 2;   // 16 KB
+  static constexpr uint32_t HALF_BYTES = QT_BYTES / 2;
+  static constexpr uint32_t DS_BYTES = BN * BT * 2;  // 32 KB: two [128 keys x 64 queries] slabs
+  static constexpr uint32_t DS_SLAB = DS_BYTES / 2;
+  static constexpr uint32_t DQS_BYTES = BT * D * 4;  // 32 KB fp32 staging
+  static constexpr uint32_t OFF_K = 0;
+  static constexpr uint32_t OFF_V = OFF_K + KV_BYTES;
+  static constexpr uint32_t OFF_Q = OFF_V + KV_BYTES;          // 2 stages
+  static constexpr uint32_t OFF_DO = OFF_Q + 2 * QT_BYTES;     // 2 stages
+  static constexpr uint32_t OFF_DS = OFF_DO + 2 * QT_BYTES;    // 2 buffers
+  static constexpr uint32_t OFF_DQS = OFF_DS + 2 * DS_BYTES;
+  static constexpr uint32_t OFF_LSE = OFF_DQS + DQS_BYTES;     // 2 stages x 128 fp32
+  static constexpr uint32_t OFF_DEL = OFF_LSE + 2 * BT * 4;
+  static constexpr uint32_t OFF_BAR = OFF_DEL + 2 * BT * 4;
+  static constexpr uint32_t SMEM_BYTES = OFF_BAR + 256 + 1024;
+  static constexpr uint32_t TMEM_COLS = 512;
+  static constexpr uint32_t COL_S0 = 0, COL_DP0 = 64, COL_S1 = 128, COL_DP1 = 192;
+  static constexpr uint32_t COL_DK = 256, COL_DV = 320, COL_DQ = 384;
+  static constexpr int THREADS = 448;
+};
+static_assert(BwdCfg::SMEM_BYTES <= 232448, "shared memory budget");
+
+struct BwdArgs {
+  Problem p;
+  TensorRef dk, dv;
+  const float* lse;
+  const float* delta;
+  float* dq_accum;    // fp32, [B][Hq][rows_pad][D] dense or [Hq][T + 128][D] packed; zeroed
+  int64_t dq_rows;    // rows_pad (dense) or T + 128 (packed) per head
+  float* dn_part;     // [B][Hq][nkv][2 halves][4 warps]
+  float* db_part;
+  unsigned int* status;
+  int nkv;            // key blocks per sequence (ceil(max_seqlen / 128))
+};
+
+enum BwdBar : int {
+  BB_KV = 0,
+  BB_QF = 1,    // 2 stages: Q/dO tile + lse/delta landed
+  BB_QE = 3,    // 2 stages: tile's MMAs retired
+  BB_SF = 5,    // 2 halves: S^T and dP^T in TMEM
+  BB_SM = 7,    // 2 halves: P^T / dS^T written (TMEM + smem)
+  BB_BF = 9,    // 2 halves: dV/dK MMAs of the half retired
+  BB_DSF = 11,  // 2 dS buffers: dQ MMA retired
+  BB_DQF = 13,  // dQ in TMEM
+  BB_DQE = 14,  // dQ read out of TMEM
+  BB_KVD = 15,  // all MMAs retired: dK, dV final
+  BB_END = 16,
+  BB_COUNT = 17
+};
+
+template <bool BF16>
+__global__ void __launch_bounds__(448, 1)
+    bwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ,
+                     const __grid_constant__ CUtensorMap tmK,
+                     const __grid_constant__ CUtensorMap tmV,
+                     const __grid_constant__ CUtensorMap tmDO, const BwdArgs a) {
+  using C = BwdCfg;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t bar0 = sbase + C::OFF_BAR;
+  auto bar = [&](int i) -> uint32_t { return bar0 + 8u * (uint32_t)i; };
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_BAR + 8 * BB_COUNT);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* lse_s = reinterpret_cast<float*>(smem + C::OFF_LSE);
+  float* del_s = reinterpret_cast<float*>(smem + C::OFF_DEL);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const Problem& p = a.p;
+  const int BHkv = p.B * p.Hkv;
+  const int kvb = (int)(blockIdx.x / BHkv);  // key block 0 (most query tiles) first
+  const int bh = blockIdx.x % BHkv;
+  const int z = bh / p.Hkv, hkv = bh % p.Hkv;
+  int seq_start, L;
+  seq_bounds(p, z, seq_start, L);
+  const int n0 = kvb * C::BN;
+  if (n0 >= L || *reinterpret_cast<volatile unsigned int*>(a.status) != 0) {
+    if (threadIdx.x < 8 * p.gqa) {  // keep the dn/db partials of an empty block well defined
+      const int g = threadIdx.x >> 3, sub = threadIdx.x & 7;
+      const int64_t pi = ((int64_t)z * p.Hq + hkv * p.gqa + g) * (8 * a.nkv) + 8 * kvb + sub;
+      a.dn_part[pi] = 0.f;
+      a.db_part[pi] = 0.f;
+    }
+    return;
+  }
+  const int q_start = p.causal ? n0 : 0;
+  const int T_h = (L - q_start + C::BT - 1) / C::BT;  // query tiles per q-head
+  const int T = T_h * p.gqa;
+  const int zc = p.cu_seqlens ? 0 : z;
+
+  if (threadIdx.x == 0) {
+    mbar_init(bar(BB_KV), 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(bar(BB_QF + s), 33);
+      mbar_init(bar(BB_QE + s), 1);
+      mbar_init(bar(BB_SF + s), 1);
+      mbar_init(bar(BB_SM + s), 128);
+      mbar_init(bar(BB_BF + s), 1);
+      mbar_init(bar(BB_DSF + s), 1);
+    }
+    mbar_init(bar(BB_DQF), 1);
+    mbar_init(bar(BB_DQE), 128);
+    mbar_init(bar(BB_KVD), 1);
+    mbar_init(bar(BB_END), 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    __syncwarp();
+    tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- producer (whole warp)
+    if (lane == 0) {
+      prefetch_tmap(&tmQ);
+      prefetch_tmap(&tmK);
+      prefetch_tmap(&tmV);
+      prefetch_tmap(&tmDO);
+      mbar_expect_tx(bar(BB_KV), 2 * C::KV_BYTES);
+      tma_load_4d(sbase + C::OFF_K, &tmK, bar(BB_KV), 0, seq_start + n0, hkv, zc);
+      tma_load_4d(sbase + C::OFF_V, &tmV, bar(BB_KV), 0, seq_start + n0, hkv, zc);
+    }
+    int last_tile = -1;
+    for (int t = 0; t < T; ++t) {
+      const int st = t & 1, u = t >> 1;
+      const int g = t / T_h, tt = t - g * T_h;
+      const int hq = hkv * p.gqa + g;
+      const int m0 = q_start + tt * C::BT;
+      bool ok = true;
+      if (t >= 2) ok = mbar_wait(bar(BB_QE + st), (u - 1) & 1, a.status);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok || *abort_flag) {
+        *abort_flag = 1;
+        break;
+      }
+      if (lane == 0) {
+        mbar_expect_tx(bar(BB_QF + st), 2 * C::QT_BYTES);
+        tma_load_4d(sbase + C::OFF_Q + st * C::QT_BYTES, &tmQ, bar(BB_QF + st), 0,
+                    seq_start + m0, hq, zc);
+        tma_load_4d(sbase + C::OFF_DO + st * C::QT_BYTES, &tmDO, bar(BB_QF + st), 0,
+                    seq_start + m0, hq, zc);
+      }
+      for (int i = lane; i < C::BT; i += 32) {
+        const int row = m0 + i;
+        float lv = 0.f, dv = 0.f;
+        if (row < L) {
+          const int64_t o = stat_offset(p, z, hq, seq_start, row);
+          lv = __ldg(a.lse + o);
+          dv = __ldg(a.delta + o);
+        }
+        lse_s[st * C::BT + i] = lv;
+        del_s[st * C::BT + i] = dv;
+      }
+      mbar_arrive(bar(BB_QF + st));
+      last_tile = t;
+    }
+    if (*abort_flag && lane == 0) {  // drain own TMA loads before shared memory is released
+      mbar_wait(bar(BB_KV), 0, a.status);
+      for (int t = max(0, last_tile - 1); t <= last_tile; ++t)
+        mbar_wait(bar(BB_QF + (t & 1)), (t >> 1) & 1, a.status);
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t id_s = idesc_f16(BF16, false, false, 128, 64);  // S^T, dP^T
+      constexpr uint32_t id_g = idesc_f16(BF16, false, true, 128, 64);   // dV, dK
+      constexpr uint32_t id_q = idesc_f16(BF16, true, true, 128, 64);    // dQ
+      const uint32_t sK = sbase + C::OFF_K, sV = sbase + C::OFF_V;
+      auto issue_sdp = [&](int t, int h) {
+        const int st = t & 1;
+        const uint32_t qb = sbase + C::OFF_Q + st * C::QT_BYTES + h * C::HALF_BYTES;
+        const uint32_t db = sbase + C::OFF_DO + st * C::QT_BYTES + h * C::HALF_BYTES;
+        const uint32_t cs = h ? C::COL_S1 : C::COL_S0, cdp = h ? C::COL_DP1 : C::COL_DP0;
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          mma_ss(tmem + cs, sdesc_sw128(sK + kk * 32, 16, 1024), sdesc_sw128(qb + kk * 32, 16, 1024),
+                 id_s, kk > 0 ? 1u : 0u);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          mma_ss(tmem + cdp, sdesc_sw128(sV + kk * 32, 16, 1024),
+                 sdesc_sw128(db + kk * 32, 16, 1024), id_s, kk > 0 ? 1u : 0u);
+        mma_commit(bar(BB_SF + h));
+      };
+      bool ok = mbar_wait(bar(BB_KV), 0, a.status) && mbar_wait(bar(BB_QF), 0, a.status);
+      if (ok) {
+        tc_fence_after();
+        issue_sdp(0, 0);
+        issue_sdp(0, 1);
+      }
+      for (int t = 0; ok && t < T; ++t) {
+        const int st = t & 1;
+        for (int h = 0; h < 2 && ok; ++h) {
+          ok = mbar_wait(bar(BB_SM + h), t & 1, a.status);
+          if (!ok || *abort_flag) break;
+          tc_fence_after();
+          const uint32_t qb = sbase + C::OFF_Q + st * C::QT_BYTES + h * C::HALF_BYTES;
+          const uint32_t db = sbase + C::OFF_DO + st * C::QT_BYTES + h * C::HALF_BYTES;
+          const uint32_t cs = h ? C::COL_S1 : C::COL_S0, cdp = h ? C::COL_DP1 : C::COL_DP0;
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            mma_ts(tmem + C::COL_DV, tmem + cs + kk * 8, sdesc_sw128(db + kk * 2048, 8192, 1024),
+                   id_g, (t > 0 || h > 0 || kk > 0) ? 1u : 0u);
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)
+            mma_ts(tmem + C::COL_DK, tmem + cdp + kk * 8, sdesc_sw128(qb + kk * 2048, 8192, 1024),
+                   id_g, (t > 0 || h > 0 || kk > 0) ? 1u : 0u);
+          mma_commit(bar(BB_BF + h));
+          if (t + 1 < T) {
+            if (h == 0) ok = mbar_wait(bar(BB_QF + ((t + 1) & 1)), ((t + 1) >> 1) & 1, a.status);
+            if (ok) ok = mbar_wait(bar(BB_BF + h), t & 1, a.status);  // P^T/dS^T consumed
+            if (!ok) break;
+            tc_fence_after();
+            issue_sdp(t + 1, h);
+          }
+        }
+        if (!ok || *abort_flag) break;
+        if (t >= 1) ok = mbar_wait(bar(BB_DQE), (t - 1) & 1, a.status);
+        if (!ok) break;
+        tc_fence_after();
+        const uint32_t ds = sbase + C::OFF_DS + st * C::DS_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          mma_ss(tmem + C::COL_DQ, sdesc_sw128(ds + kk * 2048, C::DS_SLAB, 1024),
+                 sdesc_sw128(sK + kk * 2048, 8192, 1024), id_q, kk > 0 ? 1u : 0u);
+        mma_commit(bar(BB_DQF));
+        mma_commit(bar(BB_DSF + st));
+        mma_commit(bar(BB_QE + st));
+      }
+      if (!ok) *abort_flag = 1;
+      mma_commit(bar(BB_KVD));
+      mma_commit(bar(BB_END));
+      mbar_wait(bar(BB_END), 0, a.status);
+    }
+  } else if (warp < 10) {
+    // ---------------------------------------------------------------- P / dS warp-groups
+    const int h = (warp - 2) >> 2;  // 0: warps 2..5, 1: warps 6..9
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;  // key row within the block
+    const int j = n0 + r;
+    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    const uint32_t tS = tmem + lane_off + (h ? C::COL_S1 : C::COL_S0);
+    const uint32_t tP = tmem + lane_off + (h ? C::COL_DP1 : C::COL_DP0);
+    const float bval = __ldg(p.b_ptr);
+    const float cb = bval * p.scale;
+    float n = 0.f, nbs = 0.f;
+    float dn_acc = 0.f, db_acc = 0.f;
+    bool ok = true;
+    for (int t = 0; t < T; ++t) {
+      const int st = t & 1;
+      const int g = t / T_h, tt = t - g * T_h;
+      const int hq = hkv * p.gqa + g;
+      if (tt == 0) {
+        n = load_n(p, hq);
+        nbs = n * bval * p.scale;
+      }
+      const int mh = q_start + tt * C::BT + h * 64;  // first query row of this half
+      ok = mbar_wait(bar(BB_QF + st), (t >> 1) & 1, a.status);
+      if (ok) ok = mbar_wait(bar(BB_SF + h), t & 1, a.status);
+      if (ok && t >= 2) ok = mbar_wait(bar(BB_DSF + st), ((t >> 1) - 1) & 1, a.status);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok || *abort_flag) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const bool full = (!p.causal || mh >= n0 + C::BN - 1) && (mh + 64 <= L) && (n0 + C::BN <= L);
+      const float* lrow = lse_s + st * C::BT + h * 64;
+      const float* drow = del_s + st * C::BT + h * 64;
+      uint8_t* dsrow = smem + C::OFF_DS + st * C::DS_BYTES + h * C::DS_SLAB + r * 128;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        uint32_t sx[32], dp[32];
+        tmem_ld32(tS + c * 32, sx);
+        tmem_ld32(tP + c * 32, dp);
+        tmem_ld_wait_only();
+        tmem_pin(sx);
+        tmem_pin(dp);
+        uint32_t pk[16], dk[16];
+#pragma unroll
+        for (int e4 = 0; e4 < 8; ++e4) {
+          const float4 lv = *reinterpret_cast<const float4*>(lrow + c * 32 + e4 * 4);
+          const float4 dv = *reinterpret_cast<const float4*>(drow + c * 32 + e4 * 4);
+          const float lse4[4] = {lv.x, lv.y, lv.z, lv.w};
+          const float del4[4] = {dv.x, dv.y, dv.z, dv.w};
+          float pv[4], dsv[4];
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            const int e = e4 * 4 + i;
+            const float x = __uint_as_float(sx[e]);
+            const float a1 = fmaf(fabsf(x), cb, 1.0f);
+            const float sl = copy_sign_bit(lg2_approx(a1), x);
+            float pr = ex2_approx(fmaf(n, sl, -lse4[i]));
+            if (!full) {
+              const int q = mh + c * 32 + e;
+              const bool valid = (q < L) && (j < L) && (!p.causal || j <= q);
+              pr = valid ? pr : 0.f;
+            }
+            const float dss = pr * (__uint_as_float(dp[e]) - del4[i]);
+            const float w = dss * rcp_approx(a1);
+            dn_acc = fmaf(dss, sl, dn_acc);
+            db_acc = fmaf(w, x, db_acc);
+            pv[i] = pr;
+            dsv[i] = w * nbs;
+          }
+          pk[e4 * 2] = pack2<BF16>(pv[0], pv[1]);
+          pk[e4 * 2 + 1] = pack2<BF16>(pv[2], pv[3]);
+          dk[e4 * 2] = pack2<BF16>(dsv[0], dsv[1]);
+          dk[e4 * 2 + 1] = pack2<BF16>(dsv[2], dsv[3]);
+        }
+        tmem_st16(tS + c * 16, pk);
+        tmem_st16(tP + c * 16, dk);
+        // dS^T row r of this half's slab: 16-byte chunks, 128-byte swizzle (chunk ^ (row & 7))
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+          const int chunk = c * 4 + q4;
+          *reinterpret_cast<uint4*>(dsrow + ((chunk ^ (r & 7)) << 4)) =
+              make_uint4(dk[q4 * 4], dk[q4 * 4 + 1], dk[q4 * 4 + 2], dk[q4 * 4 + 3]);
+        }
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      fence_proxy_async_smem();
+      mbar_arrive(bar(BB_SM + h));
+      if (tt == T_h - 1) {  // end of q-head g: each warp writes its dn/db partial
+        float x1 = dn_acc, x2 = db_acc;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          x1 += __shfl_xor_sync(0xffffffffu, x1, o);
+          x2 += __shfl_xor_sync(0xffffffffu, x2, o);
+        }
+        if (lane == 0) {
+          const int64_t pi = ((int64_t)z * p.Hq + hq) * (8 * a.nkv) + 8 * kvb + 4 * h + quad;
+          a.dn_part[pi] = x1 * kLn2;
+          a.db_part[pi] = x2 * n * p.scale;
+        }
+        dn_acc = 0.f;
+        db_acc = 0.f;
+      }
+    }
+    if (!ok) *abort_flag = 1;
+    // ---- epilogue: half 0 stores dK, half 1 stores dV (one key row per thread)
+    bool okd = ok && mbar_wait(bar(BB_KVD), 0, a.status);
+    okd = __all_sync(0xffffffffu, okd);
+    if (okd && !*abort_flag) {
+      tc_fence_after();
+      using Tout = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+      const TensorRef& dst = h ? a.dv : a.dk;
+      Tout* rowp = reinterpret_cast<Tout*>(dst.ptr) + row_offset(dst, p, z, hkv, seq_start, j);
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        uint32_t o[32];
+        tmem_ld32(tmem + lane_off + (h ? C::COL_DV : C::COL_DK) + c * 32, o);
+        tmem_ld_wait(o);
+        if (j < L) {
+          uint32_t w[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            w[i] = pack2<BF16>(__uint_as_float(o[2 * i]), __uint_as_float(o[2 * i + 1]));
+          uint4* d4 = reinterpret_cast<uint4*>(rowp + c * 32);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) d4[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+        }
+      }
+    }
+  } else {
+    // ---------------------------------------------------------------- dQ drain (warps 10..13)
+    // Each warp drains its own 32 query rows: TMEM -> its 8 KB of the staging buffer -> one
+    // bulk reduce-add of 8 KB (the 32 rows are contiguous in the dQ accumulator).
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;  // query row within the tile
+    const uint32_t tQ = tmem + ((uint32_t)(quad * 32) << 16) + C::COL_DQ;
+    float* stage = reinterpret_cast<float*>(smem + C::OFF_DQS) + quad * 32 * C::D;
+    const uint32_t stage_s = sbase + C::OFF_DQS + quad * 32 * C::D * 4;
+    bool ok = true;
+    for (int t = 0; t < T; ++t) {
+      ok = mbar_wait(bar(BB_DQF), t & 1, a.status);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok || *abort_flag) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t v0[32], v1[32];
+      tmem_ld32(tQ, v0);
+      tmem_ld32(tQ + 32, v1);
+      tmem_ld_wait_only();
+      tmem_pin(v0);
+      tmem_pin(v1);
+      tc_fence_before();
+      mbar_arrive(bar(BB_DQE));
+      if (lane == 0) bulk_wait_read0();  // this warp's staging rows are free again
+      __syncwarp();
+      uint4* srow = reinterpret_cast<uint4*>(stage + lane * C::D);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) srow[i] = make_uint4(v0[4 * i], v0[4 * i + 1], v0[4 * i + 2], v0[4 * i + 3]);
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        srow[8 + i] = make_uint4(v1[4 * i], v1[4 * i + 1], v1[4 * i + 2], v1[4 * i + 3]);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        const int g = t / T_h, tt = t - g * T_h;
+        const int hq = hkv * p.gqa + g;
+        const int m0 = q_start + tt * C::BT + quad * 32;
+        const int64_t row0 = p.cu_seqlens ? (int64_t)hq * a.dq_rows + seq_start + m0
+                                          : ((int64_t)z * p.Hq + hq) * a.dq_rows + m0;
+        bulk_reduce_add_f32(a.dq_accum + row0 * C::D, stage_s, 32 * C::D * 4);
+        bulk_commit();
+      }
+    }
+    if (!ok) *abort_flag = 1;
+    if (lane == 0) bulk_wait0();
+    (void)r;
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
+// dq (q's dtype, caller strides) = dq_accum (fp32) for the valid rows.
+template <typename T>
+__global__ void __launch_bounds__(256) dq_convert_kernel(Problem p, const float* dq_accum,
+                                                         int64_t dq_rows, TensorRef dq) {
+  const int z = blockIdx.y / p.Hq, hq = blockIdx.y % p.Hq;
+  int seq_start, L;
+  seq_bounds(p, z, seq_start, L);
+  const int row = blockIdx.x * 32 + (threadIdx.x >> 3);
+  const int d0 = (threadIdx.x & 7) * 8;
+  if (row >= L) return;
+  const int64_t src_row = p.cu_seqlens ? (int64_t)hq * dq_rows + seq_start + row
+                                       : ((int64_t)z * p.Hq + hq) * dq_rows + row;
+  const float4* s = reinterpret_cast<const float4*>(dq_accum + src_row * 64 + d0);
+  const float4 a0 = s[0], a1 = s[1];
+  T* d = reinterpret_cast<T*>(dq.ptr) + row_offset(dq, p, z, hq, seq_start, row) + d0;
+  uint4 w;
+  if constexpr (std::is_same<T, __nv_bfloat16>::value) {
+    w = make_uint4(pack2<true>(a0.x, a0.y), pack2<true>(a0.z, a0.w), pack2<true>(a1.x, a1.y),
+                   pack2<true>(a1.z, a1.w));
+  } else {
+    w = make_uint4(pack2<false>(a0.x, a0.y), pack2<false>(a0.z, a0.w), pack2<false>(a1.x, a1.y),
+                   pack2<false>(a1.z, a1.w));
+  }
+  *reinterpret_cast<uint4*>(d) = w;
+}
+
+struct BwdLayout {
+  int nkv;
+  int64_t dq_rows;
+  size_t dq_bytes, part_bytes, total;
+};
+
+inline size_t al256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
+
+BwdLayout bwd_layout(const Problem& p) {
+  BwdLayout l;
+  l.nkv = (p.max_seqlen + BwdCfg::BN - 1) / BwdCfg::BN;
+  if (p.cu_seqlens) {
+    l.dq_rows = (int64_t)p.N + BwdCfg::BT;
+    l.dq_bytes = al256(sizeof(float) * (size_t)p.Hq * l.dq_rows * BwdCfg::D);
+  } else {
+    l.dq_rows = (int64_t)((p.N + BwdCfg::BT - 1) / BwdCfg::BT) * BwdCfg::BT;
+    l.dq_bytes = al256(sizeof(float) * (size_t)p.B * p.Hq * l.dq_rows * BwdCfg::D);
+  }
+  l.part_bytes = al256(sizeof(float) * (size_t)p.B * p.Hq * 8 * l.nkv);
+  l.total = l.dq_bytes + 2 * l.part_bytes;
+  return l;
+}
+
+template <bool BF16>
+int run_bwd(const Problem& p, TensorRef q, TensorRef k, TensorRef v, TensorRef dout,
+            const float* lse, const float* delta, TensorRef dq, TensorRef dk, TensorRef dv,
+            float* dn, float* db, void* ws, size_t ws_bytes, cudaStream_t st) {
+  using C = BwdCfg;
+  const int dtype = BF16 ? SSA_DTYPE_BF16 : SSA_DTYPE_F16;
+  const BwdLayout lay = bwd_layout(p);
+  if (!ws || ws_bytes < lay.total) return SSA_ERR_WORKSPACE;
+  CUtensorMap tq, tk, tv, tdo;
+  int rc;
+  if ((rc = make_tmap_bhnd(&tq, q, p, dtype, p.Hq, C::BT)) != SSA_OK) return rc;
+  if ((rc = make_tmap_bhnd(&tk, k, p, dtype, p.Hkv, C::BN)) != SSA_OK) return rc;
+  if ((rc = make_tmap_bhnd(&tv, v, p, dtype, p.Hkv, C::BN)) != SSA_OK) return rc;
+  if ((rc = make_tmap_bhnd(&tdo, dout, p, dtype, p.Hq, C::BT)) != SSA_OK) return rc;
+  uint8_t* w = static_cast<uint8_t*>(ws);
+  BwdArgs a;
+  a.p = p;
+  a.dk = dk;
+  a.dv = dv;
+  a.lse = lse;
+  a.delta = delta;
+  a.dq_accum = reinterpret_cast<float*>(w);
+  a.dq_rows = lay.dq_rows;
+  a.dn_part = reinterpret_cast<float*>(w + lay.dq_bytes);
+  a.db_part = reinterpret_cast<float*>(w + lay.dq_bytes + lay.part_bytes);
+  a.status = device_status_ptr();
+  a.nkv = lay.nkv;
+  if (cudaMemsetAsync(a.dq_accum, 0, lay.dq_bytes, st) != cudaSuccess) return SSA_ERR_CUDA;
+  auto kern = bwd_sm100_kernel<BF16>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)C::SMEM_BYTES) != cudaSuccess)
+    return SSA_ERR_CUDA;
+  const long long grid = (long long)lay.nkv * p.B * p.Hkv;
+  kern<<<(unsigned)grid, C::THREADS, C::SMEM_BYTES, st>>>(tq, tk, tv, tdo, a);
+  using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+  dim3 gc((p.max_seqlen + 31) / 32, p.B * p.Hq);
+  dq_convert_kernel<T><<<gc, 256, 0, st>>>(p, a.dq_accum, a.dq_rows, dq);
+  note_launches(2);
+  return launch_dndb_reduce(a.dn_part, a.db_part, p.B, p.Hq, 8 * lay.nkv, p.n_per_head, dn, db,
+                            st);
+}
+
+}  // namespace sm100
 
 bool sm100_bwd_supports(int dtype, int D) {
-  (void)dtype;
-  (void)D;
-  return false;
+  return (dtype == SSA_DTYPE_BF16 || dtype == SSA_DTYPE_F16) && D == 64;
 }
 
-size_t sm100_bwd_workspace_bytes(const Problem& p) {
-  (void)p;
-  return 0;
-}
+size_t sm100_bwd_workspace_bytes(const Problem& p) { return sm100::bwd_layout(p).total; }
 
 int launch_bwd_sm100(int dtype, const Problem& p, TensorRef q, TensorRef k, TensorRef v,
                      TensorRef dout, const float* lse, const float* delta, TensorRef dq,
                      TensorRef dk, TensorRef dv, float* dn, float* db, void* ws, size_t ws_bytes,
                      cudaStream_t st) {
-  return SSA_ERR_UNSUPPORTED;
+  if (p.D != 64) return SSA_ERR_UNSUPPORTED;
+  return dtype == SSA_DTYPE_BF16
+             ? sm100::run_bwd<true>(p, q, k, v, dout, lse, delta, dq, dk, dv, dn, db, ws, ws_bytes, st)
+             : sm100::run_bwd<false>(p, q, k, v, dout, lse, delta, dq, dk, dv, dn, db, ws, ws_bytes, st);
 }
 
 }  // namespace ssa

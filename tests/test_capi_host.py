@@ -90,9 +90,12 @@ def test_bwd_workspace_requirement_enforced(lib):
     t = _lib.SsaTensor(16, 0, 0, 0)
     rc = lib.ssa_attn_bwd(ctypes.byref(prob), t, t, t, t, t, 16, t, t, t, 16, 16, 16, need - 1, None)
     assert rc == _lib.SSA_ERR_WORKSPACE
-    # fp32 generic workspace also holds the dn/db partials
+    # tensor-core path: delta + the fp32 dQ accumulator (B*Hq*N*D*4) + dn/db partials
+    assert need >= 8 * 2 * 256 * 4 + 2 * 8 * 256 * 64 * 4
+    # generic path: delta + dn/db partials only
     p32 = _prob(dtype=0)
-    assert lib.ssa_attn_bwd_workspace_size(ctypes.byref(p32)) >= need
+    need32 = lib.ssa_attn_bwd_workspace_size(ctypes.byref(p32))
+    assert 8 * 2 * 256 * 4 <= need32 < need
 
 
 def test_python_layer_rejects_cpu_tensors():

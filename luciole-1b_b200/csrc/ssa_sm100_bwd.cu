@@ -96,6 +96,47 @@ enum BwdBar : int {
   BB_COUNT = 17
 };
 
+// One 16-query chunk of one key row: recompute P from S, dS = P (dP - delta) n b scale / (1+u),
+// accumulate dn/db, and pack P and dS to 16 bits. MASKED adds the causal / bounds test
+// (valid iff the row is in range and qmin <= q < L).
+template <bool BF16, bool MASKED>
+__device__ __forceinline__ void bwd_chunk16(const uint32_t (&sx)[16], const uint32_t (&dp)[16],
+                                            const float* lrow, const float* drow, float n,
+                                            float cb, float nbs, int q0, int qmin, int L,
+                                            bool row_ok, float& dn_acc, float& db_acc,
+                                            uint32_t (&pk)[8], uint32_t (&dk)[8]) {
+#pragma unroll
+  for (int e4 = 0; e4 < 4; ++e4) {
+    const float4 lv = *reinterpret_cast<const float4*>(lrow + e4 * 4);
+    const float4 dv = *reinterpret_cast<const float4*>(drow + e4 * 4);
+    const float lse4[4] = {lv.x, lv.y, lv.z, lv.w};
+    const float del4[4] = {dv.x, dv.y, dv.z, dv.w};
+    float pv[4], dsv[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const int e = e4 * 4 + i;
+      const float x = __uint_as_float(sx[e]);
+      const float a1 = fmaf(fabsf(x), cb, 1.0f);
+      const float sl = copy_sign_bit(lg2_approx(a1), x);
+      float pr = ex2_approx(fmaf(n, sl, -lse4[i]));
+      if (MASKED) {
+        const int q = q0 + e;
+        pr = (row_ok && q >= qmin && q < L) ? pr : 0.f;
+      }
+      const float dss = pr * (__uint_as_float(dp[e]) - del4[i]);
+      const float w = dss * rcp_approx(a1);
+      dn_acc = fmaf(dss, sl, dn_acc);
+      db_acc = fmaf(w, x, db_acc);
+      pv[i] = pr;
+      dsv[i] = w * nbs;
+    }
+    pk[e4 * 2] = pack2<BF16>(pv[0], pv[1]);
+    pk[e4 * 2 + 1] = pack2<BF16>(pv[2], pv[3]);
+    dk[e4 * 2] = pack2<BF16>(dsv[0], dsv[1]);
+    dk[e4 * 2 + 1] = pack2<BF16>(dsv[2], dsv[3]);
+  }
+}
+
 template <bool BF16>
 __global__ void __launch_bounds__(448, 1)
     bwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ,
@@ -322,54 +363,45 @@ __global__ void __launch_bounds__(448, 1)
       const float* lrow = lse_s + st * C::BT + h * 64;
       const float* drow = del_s + st * C::BT + h * 64;
       uint8_t* dsrow = smem + C::OFF_DS + st * C::DS_BYTES + h * C::DS_SLAB + r * 128;
+      const int qmin = p.causal ? j : 0;
+      // 4 chunks of 16 queries; chunk c+1's S / dP loads are in flight while chunk c computes.
+      uint32_t sxa[16], dpa[16], sxb[16], dpb[16];
+      tmem_ld16(tS, sxa);
+      tmem_ld16(tP, dpa);
+      tmem_ld_wait_only();
+      tmem_pin_n(sxa);
+      tmem_pin_n(dpa);
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        uint32_t sx[32], dp[32];
-        tmem_ld32(tS + c * 32, sx);
-        tmem_ld32(tP + c * 32, dp);
-        tmem_ld_wait_only();
-        tmem_pin(sx);
-        tmem_pin(dp);
-        uint32_t pk[16], dk[16];
-#pragma unroll
-        for (int e4 = 0; e4 < 8; ++e4) {
-          const float4 lv = *reinterpret_cast<const float4*>(lrow + c * 32 + e4 * 4);
-          const float4 dv = *reinterpret_cast<const float4*>(drow + c * 32 + e4 * 4);
-          const float lse4[4] = {lv.x, lv.y, lv.z, lv.w};
-          const float del4[4] = {dv.x, dv.y, dv.z, dv.w};
-          float pv[4], dsv[4];
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            const int e = e4 * 4 + i;
-            const float x = __uint_as_float(sx[e]);
-            const float a1 = fmaf(fabsf(x), cb, 1.0f);
-            const float sl = copy_sign_bit(lg2_approx(a1), x);
-            float pr = ex2_approx(fmaf(n, sl, -lse4[i]));
-            if (!full) {
-              const int q = mh + c * 32 + e;
-              const bool valid = (q < L) && (j < L) && (!p.causal || j <= q);
-              pr = valid ? pr : 0.f;
-            }
-            const float dss = pr * (__uint_as_float(dp[e]) - del4[i]);
-            const float w = dss * rcp_approx(a1);
-            dn_acc = fmaf(dss, sl, dn_acc);
-            db_acc = fmaf(w, x, db_acc);
-            pv[i] = pr;
-            dsv[i] = w * nbs;
-          }
-          pk[e4 * 2] = pack2<BF16>(pv[0], pv[1]);
-          pk[e4 * 2 + 1] = pack2<BF16>(pv[2], pv[3]);
-          dk[e4 * 2] = pack2<BF16>(dsv[0], dsv[1]);
-          dk[e4 * 2 + 1] = pack2<BF16>(dsv[2], dsv[3]);
+      for (int c = 0; c < 4; ++c) {
+        uint32_t(&cs)[16] = (c & 1) ? sxb : sxa;
+        uint32_t(&cd)[16] = (c & 1) ? dpb : dpa;
+        uint32_t(&ns)[16] = (c & 1) ? sxa : sxb;
+        uint32_t(&nd)[16] = (c & 1) ? dpa : dpb;
+        if (c < 3) {
+          tmem_ld16(tS + (c + 1) * 16, ns);
+          tmem_ld16(tP + (c + 1) * 16, nd);
         }
-        tmem_st16(tS + c * 16, pk);
-        tmem_st16(tP + c * 16, dk);
+        uint32_t pk[8], dk[8];
+        if (full)
+          bwd_chunk16<BF16, false>(cs, cd, lrow + c * 16, drow + c * 16, n, cb, nbs, mh + c * 16,
+                                   qmin, L, j < L, dn_acc, db_acc, pk, dk);
+        else
+          bwd_chunk16<BF16, true>(cs, cd, lrow + c * 16, drow + c * 16, n, cb, nbs, mh + c * 16,
+                                  qmin, L, j < L, dn_acc, db_acc, pk, dk);
+        // P^T / dS^T (packed) overwrite columns [8c, 8c+8), loaded by an earlier chunk.
+        tmem_st8(tS + c * 8, pk);
+        tmem_st8(tP + c * 8, dk);
         // dS^T row r of this half's slab: 16-byte chunks, 128-byte swizzle (chunk ^ (row & 7))
 #pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
-          const int chunk = c * 4 + q4;
+        for (int q2 = 0; q2 < 2; ++q2) {
+          const int chunk = c * 2 + q2;
           *reinterpret_cast<uint4*>(dsrow + ((chunk ^ (r & 7)) << 4)) =
-              make_uint4(dk[q4 * 4], dk[q4 * 4 + 1], dk[q4 * 4 + 2], dk[q4 * 4 + 3]);
+              make_uint4(dk[q2 * 4], dk[q2 * 4 + 1], dk[q2 * 4 + 2], dk[q2 * 4 + 3]);
+        }
+        if (c < 3) {
+          tmem_ld_wait_only();
+          tmem_pin_n(ns);
+          tmem_pin_n(nd);
         }
       }
       tmem_st_wait();

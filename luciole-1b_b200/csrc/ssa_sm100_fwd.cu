@@ -14,9 +14,10 @@
 // Two CTAs share an SM (TMEM 2 x 256 columns, ~81 KB shared memory each), so one CTA's
 // transcendental work overlaps the other's tensor-core work.
 //
-// Rescaling: the running max only moves when a block's max exceeds it by more than
-// kRescaleThreshold (log2 units), so P <= 2^8 and O is corrected rarely; m, l and O always
-// refer to the same (possibly stale) max, so the result is exact up to rounding.
+// Rescaling: each block's row maximum is bounded from above by U = |n| log2(1 + b max|s|)
+// (t2 is monotone in s); the running reference only moves when U exceeds it by more than
+// kRescaleThreshold (log2 units), so P <= 2^8 and O is corrected rarely. m, l and O always
+// refer to the same reference, so the result is exact up to rounding.
 //
 // Every mbarrier wait is bounded (~1 s): on expiry the kernel records SSA_ERR_DEVICE_TIMEOUT in
 // the device status word, unwinds, waits for its own in-flight TMA / MMA work (bounded) and
@@ -217,7 +218,7 @@ __global__ void __launch_bounds__(192, 2)
     const uint32_t t_lane = tmem + ((uint32_t)(quad * 32) << 16);
     const float n = load_n(p, hq);
     const float cb = __ldg(p.b_ptr) * p.scale;  // b * |scale|; scale > 0 on this path
-    float m_run = -INFINITY, l_run = 0.f;
+    float m_run = -INFINITY, l_run = 0.f;  // m_run: reference of l and O (log2 units)
     bool ok = true;
     for (int j = 0; j < nblk; ++j) {
       ok = mbar_wait(bar(FB_S), j & 1, a.status);
@@ -236,43 +237,63 @@ __global__ void __launch_bounds__(192, 2)
 
       const int n0 = j * C::BN;
       const bool full = (n0 + C::BN <= L) && (!p.causal || n0 + C::BN - 1 <= m0);
-      float bmax = -INFINITY;
+      // Normaliser reference: t2 = n sign(s) log2(1 + b|s|) <= |n| log2(1 + b max|s|) = U, so U
+      // bounds the row's max from above without transforming every element first. Masked
+      // elements may enter the bound (they are real scores of this row, or zero padding); only
+      // the bound's tightness depends on them, never the result.
+      float am0 = 0.f, am1 = 0.f, am2 = 0.f, am3 = 0.f;
 #pragma unroll
       for (int c = 0; c < C::BN / 32; ++c) {
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const float x = __uint_as_float(sr[c][i]);
-          const float l2 = lg2_approx(fmaf(fabsf(x), cb, 1.0f));
-          float t2 = n * copy_sign_bit(l2, x);
-          if (!full) {
-            const int col = n0 + c * 32 + i;
-            const bool valid = (row < L) && (col < L) && (!p.causal || col <= row);
-            t2 = valid ? t2 : -INFINITY;
-          }
-          sr[c][i] = __float_as_uint(t2);
-          bmax = fmaxf(bmax, t2);
+        for (int i = 0; i < 32; i += 4) {
+          am0 = fmaxf(am0, fabsf(__uint_as_float(sr[c][i])));
+          am1 = fmaxf(am1, fabsf(__uint_as_float(sr[c][i + 1])));
+          am2 = fmaxf(am2, fabsf(__uint_as_float(sr[c][i + 2])));
+          am3 = fmaxf(am3, fabsf(__uint_as_float(sr[c][i + 3])));
         }
       }
-      const float m_new = fmaxf(m_run, bmax);
-      const bool need = m_new > m_run + kRescaleThreshold;
+      const float ubound = fabsf(n) * lg2_approx(fmaf(fmaxf(fmaxf(am0, am1), fmaxf(am2, am3)), cb, 1.0f));
+      const bool need = ubound > m_run + kRescaleThreshold;  // always true on the first block
       float alpha = 1.f;
       if (need) {
-        alpha = ex2_approx(m_run - m_new);
-        m_run = m_new;
+        alpha = ex2_approx(m_run - ubound);
+        m_run = ubound;
       }
-      const float m_use = (m_run == -INFINITY) ? 0.f : m_run;
-      float rs = 0.f;
+      const float neg_m = -m_run;
+      float rs0 = 0.f, rs1 = 0.f;
       uint32_t pk[C::BN / 64][32];
+      if (full) {
 #pragma unroll
-      for (int c = 0; c < C::BN / 32; ++c) {
+        for (int c = 0; c < C::BN / 32; ++c) {
 #pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          const float p0 = ex2_approx(__uint_as_float(sr[c][i]) - m_use);
-          const float p1 = ex2_approx(__uint_as_float(sr[c][i + 1]) - m_use);
-          rs += p0 + p1;
-          pk[c >> 1][(c & 1) * 16 + (i >> 1)] = pack2<BF16>(p0, p1);
+          for (int i = 0; i < 32; i += 2) {
+            const float x0 = __uint_as_float(sr[c][i]), x1 = __uint_as_float(sr[c][i + 1]);
+            const float p0 = ex2_approx(fmaf(n, copy_sign_bit(lg2_approx(fmaf(fabsf(x0), cb, 1.0f)), x0), neg_m));
+            const float p1 = ex2_approx(fmaf(n, copy_sign_bit(lg2_approx(fmaf(fabsf(x1), cb, 1.0f)), x1), neg_m));
+            rs0 += p0;
+            rs1 += p1;
+            pk[c >> 1][(c & 1) * 16 + (i >> 1)] = pack2<BF16>(p0, p1);
+          }
+        }
+      } else {
+        const int lim = p.causal ? min(L - 1, row) : L - 1;  // last visible key of this row
+#pragma unroll
+        for (int c = 0; c < C::BN / 32; ++c) {
+#pragma unroll
+          for (int i = 0; i < 32; i += 2) {
+            const int col = n0 + c * 32 + i;
+            const float x0 = __uint_as_float(sr[c][i]), x1 = __uint_as_float(sr[c][i + 1]);
+            float p0 = ex2_approx(fmaf(n, copy_sign_bit(lg2_approx(fmaf(fabsf(x0), cb, 1.0f)), x0), neg_m));
+            float p1 = ex2_approx(fmaf(n, copy_sign_bit(lg2_approx(fmaf(fabsf(x1), cb, 1.0f)), x1), neg_m));
+            p0 = (col <= lim && row < L) ? p0 : 0.f;
+            p1 = (col + 1 <= lim && row < L) ? p1 : 0.f;
+            rs0 += p0;
+            rs1 += p1;
+            pk[c >> 1][(c & 1) * 16 + (i >> 1)] = pack2<BF16>(p0, p1);
+          }
         }
       }
+      const float rs = rs0 + rs1;
       l_run = l_run * alpha + rs;
       // O correction. PV_{j-1} completed before S_j's commit fired (commit tracks every
       // earlier tcgen05 op of the issuing thread), so O is final for blocks < j here.

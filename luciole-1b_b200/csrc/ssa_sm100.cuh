@@ -214,6 +214,15 @@ __device__ __forceinline__ void bulk_reduce_add_f32(float* gdst, uint32_t ssrc, 
       "r"(ssrc), "r"(bytes)
       : "memory");
 }
+// 2-D tiled TMA reduce-add (fp32) of a shared-memory box into the tensor map's global tensor.
+__device__ __forceinline__ void tma_reduce_add_2d(const CUtensorMap* map, uint32_t ssrc, int c0,
+                                                  int c1) {
+  asm volatile(
+      "cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(ssrc), "r"(c0), "r"(c1)
+      : "memory");
+}
 __device__ __forceinline__ void bulk_commit() {
   asm volatile("cp.async.bulk.commit_group;" ::: "memory");
 }
@@ -224,6 +233,16 @@ __device__ __forceinline__ void bulk_wait_read0() {
 // All committed bulk groups have completed (global writes performed).
 __device__ __forceinline__ void bulk_wait0() {
   asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+}
+
+// Per-warpgroup register budget changes (all four warps of the warpgroup execute the same one).
+template <uint32_t N>
+__device__ __forceinline__ void regs_inc() {
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;" ::"n"(N));
+}
+template <uint32_t N>
+__device__ __forceinline__ void regs_dec() {
+  asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;" ::"n"(N));
 }
 
 // Named barrier over `count` threads (a warp-group), id 1..15 (0 is __syncthreads).

@@ -11,16 +11,17 @@
 // One CTA owns a 128-row key block of one (sequence, kv-head) and walks every q-head of its GQA
 // group (ssa_triton_kernel.py:573) and every 128-row query tile that can see the block. Per query
 // tile, the two 64-row halves are handled by two warp-groups in ping-pong:
-//   warp 0      TMA producer: K, V once; Q and dO tiles through a 2-stage ring; the tile's
+//   warp 12     TMA producer: K, V once; Q and dO tiles through a 2-stage ring; the tile's
 //               lse / delta rows into shared memory with plain loads.
-//   warp 1      MMA issuer (tcgen05, fp32 accumulation in TMEM):
+//   warp 13     MMA issuer (tcgen05, fp32 accumulation in TMEM):
 //                 S^T  = K Q_h^T,  dP^T = V dO_h^T          (SS, M=128 keys, N=64 queries)
 //                 dV  += P^T dO_h,  dK += dS^T Q_h          (TS: P^T / dS^T read from TMEM)
 //                 dQ   = dS K                               (SS, M=128 queries, dS from smem)
-//   warps 2..5  half 0 of each tile, one thread per key row: SSA transform, P, dS, dn/db
-//   warps 6..9  half 1 of each tile
-//   warps 10..13 dQ drain: TMEM -> shared staging -> one TMA bulk reduce-add (fp32) into the
+//   warps 0..3  half 0 of each tile, one thread per key row: SSA transform, P, dS, dn/db
+//   warps 4..7  half 1 of each tile
+//   warps 8..11 dQ drain: TMEM -> shared staging -> TMA bulk reduce-adds (fp32) into the
 //               dQ accumulator in global memory; a small kernel converts it to dq's dtype.
+// The roles sit on whole warpgroups so setmaxnreg can move registers to the P/dS groups.
 // TMEM (512 columns): S/dP for half 0 [0,128), for half 1 [128,256), dK [256,320),
 // dV [320,384), dQ [384,448). P^T and dS^T (packed 16-bit) overwrite the S and dP columns
 // they were computed from.
@@ -50,21 +51,30 @@ struct BwdCfg {
   static constexpr uint32_t HALF_BYTES = QT_BYTES / 2;
   static constexpr uint32_t DS_BYTES = BN * BT * 2;  // 32 KB: two [128 keys x 64 queries] slabs
   static constexpr uint32_t DS_SLAB = DS_BYTES / 2;
-  static constexpr uint32_t DQS_BYTES = BT * D * 4;  // 32 KB fp32 staging
+  static constexpr int STAGES = 3;                   // Q / dO / lse / delta ring
+  static constexpr uint32_t DQS_WARP = 32 * 32 * 4;  // 4 KB: 32 rows x 32 fp32 per drain warp
   static constexpr uint32_t OFF_K = 0;
   static constexpr uint32_t OFF_V = OFF_K + KV_BYTES;
-  static constexpr uint32_t OFF_Q = OFF_V + KV_BYTES;          // 2 stages
-  static constexpr uint32_t OFF_DO = OFF_Q + 2 * QT_BYTES;     // 2 stages
-  static constexpr uint32_t OFF_DS = OFF_DO + 2 * QT_BYTES;    // 2 buffers
-  static constexpr uint32_t OFF_DQS = OFF_DS + 2 * DS_BYTES;
-  static constexpr uint32_t OFF_LSE = OFF_DQS + DQS_BYTES;     // 2 stages x 128 fp32
-  static constexpr uint32_t OFF_DEL = OFF_LSE + 2 * BT * 4;
-  static constexpr uint32_t OFF_BAR = OFF_DEL + 2 * BT * 4;
+  static constexpr uint32_t OFF_Q = OFF_V + KV_BYTES;               // STAGES tiles
+  static constexpr uint32_t OFF_DO = OFF_Q + STAGES * QT_BYTES;     // STAGES tiles
+  static constexpr uint32_t OFF_DS = OFF_DO + STAGES * QT_BYTES;    // 2 buffers
+  static constexpr uint32_t OFF_DQS = OFF_DS + 2 * DS_BYTES;        // 4 warps x 4 KB
+  static constexpr uint32_t OFF_LSE = OFF_DQS + 4 * DQS_WARP;       // STAGES x 128 fp32
+  static constexpr uint32_t OFF_DEL = OFF_LSE + STAGES * BT * 4;
+  static constexpr uint32_t OFF_BAR = OFF_DEL + STAGES * BT * 4;
   static constexpr uint32_t SMEM_BYTES = OFF_BAR + 256 + 1024;
   static constexpr uint32_t TMEM_COLS = 512;
   static constexpr uint32_t COL_S0 = 0, COL_DP0 = 64, COL_S1 = 128, COL_DP1 = 192;
   static constexpr uint32_t COL_DK = 256, COL_DV = 320, COL_DQ = 384;
-  static constexpr int THREADS = 448;
+  static constexpr int THREADS = 512;
+  // Warp roles (warpgroup-aligned so each group can resize its register file):
+  //   warps 0..3 / 4..7  P/dS for query halves 0 / 1   (regs raised to REGS_PDS)
+  //   warps 8..11        dQ drain                       (REGS_DQ)
+  //   warp 12 TMA producer, warp 13 MMA issuer, 14..15 idle (REGS_CTRL)
+  // Budget at launch: 512 threads x 128 = 65536; after the moves 2*128*184 + 128*88 + 128*56
+  // = 65536.
+  static constexpr uint32_t REGS_PDS = 184, REGS_DQ = 88, REGS_CTRL = 56;
+  static constexpr int WARP_PRODUCER = 12, WARP_MMA = 13;
 };
 static_assert(BwdCfg::SMEM_BYTES <= 232448, "shared memory budget");
 
@@ -83,30 +93,31 @@ struct BwdArgs {
 
 enum BwdBar : int {
   BB_KV = 0,
-  BB_QF = 1,    // 2 stages: Q/dO tile + lse/delta landed
-  BB_QE = 3,    // 2 stages: tile's MMAs retired
-  BB_SF = 5,    // 2 halves: S^T and dP^T in TMEM
-  BB_SM = 7,    // 2 halves: P^T / dS^T written (TMEM + smem)
-  BB_BF = 9,    // 2 halves: dV/dK MMAs of the half retired
-  BB_DSF = 11,  // 2 dS buffers: dQ MMA retired
-  BB_DQF = 13,  // dQ in TMEM
-  BB_DQE = 14,  // dQ read out of TMEM
-  BB_KVD = 15,  // all MMAs retired: dK, dV final
-  BB_END = 16,
-  BB_COUNT = 17
+  BB_QF = 1,    // 3 stages: Q/dO tile + lse/delta landed
+  BB_QE = 4,    // 3 stages: tile's MMAs retired
+  BB_SF = 7,    // 2 halves: S^T and dP^T in TMEM
+  BB_SM = 9,    // 2 halves: P^T / dS^T written (TMEM + smem)
+  BB_BF = 11,   // 2 halves: dV/dK MMAs of the half retired
+  BB_DSF = 13,  // 2 dS buffers: dQ MMA retired
+  BB_DQF = 15,  // dQ in TMEM
+  BB_DQE = 16,  // dQ read out of TMEM
+  BB_KVD = 17,  // all MMAs retired: dK, dV final
+  BB_END = 18,
+  BB_COUNT = 19
 };
 
-// One 16-query chunk of one key row: recompute P from S, dS = P (dP - delta) n b scale / (1+u),
-// accumulate dn/db, and pack P and dS to 16 bits. MASKED adds the causal / bounds test
-// (valid iff the row is in range and qmin <= q < L).
-template <bool BF16, bool MASKED>
-__device__ __forceinline__ void bwd_chunk16(const uint32_t (&sx)[16], const uint32_t (&dp)[16],
-                                            const float* lrow, const float* drow, float n,
-                                            float cb, float nbs, int q0, int qmin, int L,
-                                            bool row_ok, float& dn_acc, float& db_acc,
-                                            uint32_t (&pk)[8], uint32_t (&dk)[8]) {
+// One W-query chunk of one key row: recompute P from S, dS = P (dP - delta) n b scale / (1+u),
+// accumulate dn/db (four independent partial sums each, to keep dependency chains short), and
+// pack P and dS to 16 bits. MASKED adds the causal / bounds test (valid iff the row is in range
+// and qmin <= q < L).
+template <int W, bool BF16, bool MASKED>
+__device__ __forceinline__ void bwd_chunk(const uint32_t (&sx)[W], const uint32_t (&dp)[W],
+                                          const float* lrow, const float* drow, float n, float cb,
+                                          float nbs, int q0, int qmin, int L, bool row_ok,
+                                          float (&dn_acc)[4], float (&db_acc)[4],
+                                          uint32_t (&pk)[W / 2], uint32_t (&dk)[W / 2]) {
 #pragma unroll
-  for (int e4 = 0; e4 < 4; ++e4) {
+  for (int e4 = 0; e4 < W / 4; ++e4) {
     const float4 lv = *reinterpret_cast<const float4*>(lrow + e4 * 4);
     const float4 dv = *reinterpret_cast<const float4*>(drow + e4 * 4);
     const float lse4[4] = {lv.x, lv.y, lv.z, lv.w};
@@ -125,8 +136,8 @@ __device__ __forceinline__ void bwd_chunk16(const uint32_t (&sx)[16], const uint
       }
       const float dss = pr * (__uint_as_float(dp[e]) - del4[i]);
       const float w = dss * rcp_approx(a1);
-      dn_acc = fmaf(dss, sl, dn_acc);
-      db_acc = fmaf(w, x, db_acc);
+      dn_acc[i] = fmaf(dss, sl, dn_acc[i]);
+      db_acc[i] = fmaf(w, x, db_acc[i]);
       pv[i] = pr;
       dsv[i] = w * nbs;
     }
@@ -138,11 +149,12 @@ __device__ __forceinline__ void bwd_chunk16(const uint32_t (&sx)[16], const uint
 }
 
 template <bool BF16>
-__global__ void __launch_bounds__(448, 1)
+__global__ void __launch_bounds__(512, 1)
     bwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ,
                      const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV,
-                     const __grid_constant__ CUtensorMap tmDO, const BwdArgs a) {
+                     const __grid_constant__ CUtensorMap tmDO,
+                     const __grid_constant__ CUtensorMap tmDQ, const BwdArgs a) {
   using C = BwdCfg;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>(
@@ -180,9 +192,11 @@ __global__ void __launch_bounds__(448, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(bar(BB_KV), 1);
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(bar(BB_QF + s), 33);
       mbar_init(bar(BB_QE + s), 1);
+    }
+    for (int s = 0; s < 2; ++s) {
       mbar_init(bar(BB_SF + s), 1);
       mbar_init(bar(BB_SM + s), 128);
       mbar_init(bar(BB_BF + s), 1);
@@ -195,7 +209,7 @@ __global__ void __launch_bounds__(448, 1)
     *abort_flag = 0;
     fence_mbar_init();
   }
-  if (warp == 0) {
+  if (warp == C::WARP_PRODUCER) {
     __syncwarp();
     tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
     tmem_relinquish();
@@ -205,7 +219,9 @@ __global__ void __launch_bounds__(448, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0) {
+  if (warp >= 12) {
+   regs_dec<C::REGS_CTRL>();
+   if (warp == C::WARP_PRODUCER) {
     // ---------------------------------------------------------------- producer (whole warp)
     if (lane == 0) {
       prefetch_tmap(&tmQ);
@@ -217,13 +233,33 @@ __global__ void __launch_bounds__(448, 1)
       tma_load_4d(sbase + C::OFF_V, &tmV, bar(BB_KV), 0, seq_start + n0, hkv, zc);
     }
     int last_tile = -1;
+    // lse / delta of the next tile are fetched into registers one tile ahead, so their global
+    // latency overlaps the wait for a free stage.
+    float pl[C::BT / 32], pd[C::BT / 32];
+    auto fetch_stats = [&](int t) {
+      const int g = t / T_h, tt = t - g * T_h;
+      const int hq = hkv * p.gqa + g;
+      const int m0 = q_start + tt * C::BT;
+#pragma unroll
+      for (int k = 0; k < C::BT / 32; ++k) {
+        const int row = m0 + lane + 32 * k;
+        pl[k] = 0.f;
+        pd[k] = 0.f;
+        if (row < L) {
+          const int64_t o = stat_offset(p, z, hq, seq_start, row);
+          pl[k] = __ldg(a.lse + o);
+          pd[k] = __ldg(a.delta + o);
+        }
+      }
+    };
+    fetch_stats(0);
     for (int t = 0; t < T; ++t) {
-      const int st = t & 1, u = t >> 1;
+      const int st = t % C::STAGES, u = t / C::STAGES;
       const int g = t / T_h, tt = t - g * T_h;
       const int hq = hkv * p.gqa + g;
       const int m0 = q_start + tt * C::BT;
       bool ok = true;
-      if (t >= 2) ok = mbar_wait(bar(BB_QE + st), (u - 1) & 1, a.status);
+      if (t >= C::STAGES) ok = mbar_wait(bar(BB_QE + st), (u - 1) & 1, a.status);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok || *abort_flag) {
         *abort_flag = 1;
@@ -236,26 +272,21 @@ __global__ void __launch_bounds__(448, 1)
         tma_load_4d(sbase + C::OFF_DO + st * C::QT_BYTES, &tmDO, bar(BB_QF + st), 0,
                     seq_start + m0, hq, zc);
       }
-      for (int i = lane; i < C::BT; i += 32) {
-        const int row = m0 + i;
-        float lv = 0.f, dv = 0.f;
-        if (row < L) {
-          const int64_t o = stat_offset(p, z, hq, seq_start, row);
-          lv = __ldg(a.lse + o);
-          dv = __ldg(a.delta + o);
-        }
-        lse_s[st * C::BT + i] = lv;
-        del_s[st * C::BT + i] = dv;
+#pragma unroll
+      for (int k = 0; k < C::BT / 32; ++k) {
+        lse_s[st * C::BT + lane + 32 * k] = pl[k];
+        del_s[st * C::BT + lane + 32 * k] = pd[k];
       }
       mbar_arrive(bar(BB_QF + st));
       last_tile = t;
+      if (t + 1 < T) fetch_stats(t + 1);
     }
     if (*abort_flag && lane == 0) {  // drain own TMA loads before shared memory is released
       mbar_wait(bar(BB_KV), 0, a.status);
-      for (int t = max(0, last_tile - 1); t <= last_tile; ++t)
-        mbar_wait(bar(BB_QF + (t & 1)), (t >> 1) & 1, a.status);
+      for (int t = max(0, last_tile - C::STAGES + 1); t <= last_tile; ++t)
+        mbar_wait(bar(BB_QF + t % C::STAGES), (t / C::STAGES) & 1, a.status);
     }
-  } else if (warp == 1) {
+   } else if (warp == C::WARP_MMA) {
     // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
       constexpr uint32_t id_s = idesc_f16(BF16, false, false, 128, 64);  // S^T, dP^T
@@ -263,7 +294,7 @@ __global__ void __launch_bounds__(448, 1)
       constexpr uint32_t id_q = idesc_f16(BF16, true, true, 128, 64);    // dQ
       const uint32_t sK = sbase + C::OFF_K, sV = sbase + C::OFF_V;
       auto issue_sdp = [&](int t, int h) {
-        const int st = t & 1;
+        const int st = t % C::STAGES;
         const uint32_t qb = sbase + C::OFF_Q + st * C::QT_BYTES + h * C::HALF_BYTES;
         const uint32_t db = sbase + C::OFF_DO + st * C::QT_BYTES + h * C::HALF_BYTES;
         const uint32_t cs = h ? C::COL_S1 : C::COL_S0, cdp = h ? C::COL_DP1 : C::COL_DP0;
@@ -284,7 +315,7 @@ __global__ void __launch_bounds__(448, 1)
         issue_sdp(0, 1);
       }
       for (int t = 0; ok && t < T; ++t) {
-        const int st = t & 1;
+        const int st = t % C::STAGES, dsb = t & 1;
         for (int h = 0; h < 2 && ok; ++h) {
           ok = mbar_wait(bar(BB_SM + h), t & 1, a.status);
           if (!ok || *abort_flag) break;
@@ -302,7 +333,8 @@ __global__ void __launch_bounds__(448, 1)
                    id_g, (t > 0 || h > 0 || kk > 0) ? 1u : 0u);
           mma_commit(bar(BB_BF + h));
           if (t + 1 < T) {
-            if (h == 0) ok = mbar_wait(bar(BB_QF + ((t + 1) & 1)), ((t + 1) >> 1) & 1, a.status);
+            if (h == 0)
+              ok = mbar_wait(bar(BB_QF + (t + 1) % C::STAGES), ((t + 1) / C::STAGES) & 1, a.status);
             if (ok) ok = mbar_wait(bar(BB_BF + h), t & 1, a.status);  // P^T/dS^T consumed
             if (!ok) break;
             tc_fence_after();
@@ -313,13 +345,13 @@ __global__ void __launch_bounds__(448, 1)
         if (t >= 1) ok = mbar_wait(bar(BB_DQE), (t - 1) & 1, a.status);
         if (!ok) break;
         tc_fence_after();
-        const uint32_t ds = sbase + C::OFF_DS + st * C::DS_BYTES;
+        const uint32_t ds = sbase + C::OFF_DS + dsb * C::DS_BYTES;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
           mma_ss(tmem + C::COL_DQ, sdesc_sw128(ds + kk * 2048, C::DS_SLAB, 1024),
                  sdesc_sw128(sK + kk * 2048, 8192, 1024), id_q, kk > 0 ? 1u : 0u);
         mma_commit(bar(BB_DQF));
-        mma_commit(bar(BB_DSF + st));
+        mma_commit(bar(BB_DSF + dsb));
         mma_commit(bar(BB_QE + st));
       }
       if (!ok) *abort_flag = 1;
@@ -327,9 +359,11 @@ __global__ void __launch_bounds__(448, 1)
       mma_commit(bar(BB_END));
       mbar_wait(bar(BB_END), 0, a.status);
     }
-  } else if (warp < 10) {
+   }
+  } else if (warp < 8) {
     // ---------------------------------------------------------------- P / dS warp-groups
-    const int h = (warp - 2) >> 2;  // 0: warps 2..5, 1: warps 6..9
+    regs_inc<C::REGS_PDS>();
+    const int h = warp >> 2;  // 0: warps 0..3, 1: warps 4..7
     const int quad = warp & 3;
     const int r = quad * 32 + lane;  // key row within the block
     const int j = n0 + r;
@@ -339,10 +373,10 @@ __global__ void __launch_bounds__(448, 1)
     const float bval = __ldg(p.b_ptr);
     const float cb = bval * p.scale;
     float n = 0.f, nbs = 0.f;
-    float dn_acc = 0.f, db_acc = 0.f;
+    float dn_acc[4] = {0.f, 0.f, 0.f, 0.f}, db_acc[4] = {0.f, 0.f, 0.f, 0.f};
     bool ok = true;
     for (int t = 0; t < T; ++t) {
-      const int st = t & 1;
+      const int st = t % C::STAGES, dsb = t & 1;
       const int g = t / T_h, tt = t - g * T_h;
       const int hq = hkv * p.gqa + g;
       if (tt == 0) {
@@ -350,9 +384,9 @@ __global__ void __launch_bounds__(448, 1)
         nbs = n * bval * p.scale;
       }
       const int mh = q_start + tt * C::BT + h * 64;  // first query row of this half
-      ok = mbar_wait(bar(BB_QF + st), (t >> 1) & 1, a.status);
+      ok = mbar_wait(bar(BB_QF + st), (t / C::STAGES) & 1, a.status);
       if (ok) ok = mbar_wait(bar(BB_SF + h), t & 1, a.status);
-      if (ok && t >= 2) ok = mbar_wait(bar(BB_DSF + st), ((t >> 1) - 1) & 1, a.status);
+      if (ok && t >= 2) ok = mbar_wait(bar(BB_DSF + dsb), ((t >> 1) - 1) & 1, a.status);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok || *abort_flag) {
         ok = false;
@@ -362,46 +396,44 @@ __global__ void __launch_bounds__(448, 1)
       const bool full = (!p.causal || mh >= n0 + C::BN - 1) && (mh + 64 <= L) && (n0 + C::BN <= L);
       const float* lrow = lse_s + st * C::BT + h * 64;
       const float* drow = del_s + st * C::BT + h * 64;
-      uint8_t* dsrow = smem + C::OFF_DS + st * C::DS_BYTES + h * C::DS_SLAB + r * 128;
+      uint8_t* dsrow = smem + C::OFF_DS + dsb * C::DS_BYTES + h * C::DS_SLAB + r * 128;
       const int qmin = p.causal ? j : 0;
-      // 4 chunks of 16 queries; chunk c+1's S / dP loads are in flight while chunk c computes.
-      uint32_t sxa[16], dpa[16], sxb[16], dpb[16];
-      tmem_ld16(tS, sxa);
-      tmem_ld16(tP, dpa);
+      // 2 chunks of 32 queries; chunk 1's S / dP loads are in flight while chunk 0 computes.
+      uint32_t sxa[32], dpa[32], sxb[32], dpb[32];
+      tmem_ld32(tS, sxa);
+      tmem_ld32(tP, dpa);
       tmem_ld_wait_only();
       tmem_pin_n(sxa);
       tmem_pin_n(dpa);
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t(&cs)[16] = (c & 1) ? sxb : sxa;
-        uint32_t(&cd)[16] = (c & 1) ? dpb : dpa;
-        uint32_t(&ns)[16] = (c & 1) ? sxa : sxb;
-        uint32_t(&nd)[16] = (c & 1) ? dpa : dpb;
-        if (c < 3) {
-          tmem_ld16(tS + (c + 1) * 16, ns);
-          tmem_ld16(tP + (c + 1) * 16, nd);
+      for (int c = 0; c < 2; ++c) {
+        uint32_t(&cs)[32] = c ? sxb : sxa;
+        uint32_t(&cd)[32] = c ? dpb : dpa;
+        if (c == 0) {
+          tmem_ld32(tS + 32, sxb);
+          tmem_ld32(tP + 32, dpb);
         }
-        uint32_t pk[8], dk[8];
+        uint32_t pk[16], dk[16];
         if (full)
-          bwd_chunk16<BF16, false>(cs, cd, lrow + c * 16, drow + c * 16, n, cb, nbs, mh + c * 16,
-                                   qmin, L, j < L, dn_acc, db_acc, pk, dk);
+          bwd_chunk<32, BF16, false>(cs, cd, lrow + c * 32, drow + c * 32, n, cb, nbs, mh + c * 32,
+                                     qmin, L, j < L, dn_acc, db_acc, pk, dk);
         else
-          bwd_chunk16<BF16, true>(cs, cd, lrow + c * 16, drow + c * 16, n, cb, nbs, mh + c * 16,
-                                  qmin, L, j < L, dn_acc, db_acc, pk, dk);
-        // P^T / dS^T (packed) overwrite columns [8c, 8c+8), loaded by an earlier chunk.
-        tmem_st8(tS + c * 8, pk);
-        tmem_st8(tP + c * 8, dk);
+          bwd_chunk<32, BF16, true>(cs, cd, lrow + c * 32, drow + c * 32, n, cb, nbs, mh + c * 32,
+                                    qmin, L, j < L, dn_acc, db_acc, pk, dk);
+        if (c == 0) {  // chunk 1 must be in registers before columns [0, 16) are overwritten
+          tmem_ld_wait_only();
+          tmem_pin_n(sxb);
+          tmem_pin_n(dpb);
+        }
+        // P^T / dS^T (packed) overwrite columns [16c, 16c+16), already loaded.
+        tmem_st16(tS + c * 16, pk);
+        tmem_st16(tP + c * 16, dk);
         // dS^T row r of this half's slab: 16-byte chunks, 128-byte swizzle (chunk ^ (row & 7))
 #pragma unroll
-        for (int q2 = 0; q2 < 2; ++q2) {
-          const int chunk = c * 2 + q2;
+        for (int q4 = 0; q4 < 4; ++q4) {
+          const int chunk = c * 4 + q4;
           *reinterpret_cast<uint4*>(dsrow + ((chunk ^ (r & 7)) << 4)) =
-              make_uint4(dk[q2 * 4], dk[q2 * 4 + 1], dk[q2 * 4 + 2], dk[q2 * 4 + 3]);
-        }
-        if (c < 3) {
-          tmem_ld_wait_only();
-          tmem_pin_n(ns);
-          tmem_pin_n(nd);
+              make_uint4(dk[q4 * 4], dk[q4 * 4 + 1], dk[q4 * 4 + 2], dk[q4 * 4 + 3]);
         }
       }
       tmem_st_wait();
@@ -409,7 +441,8 @@ __global__ void __launch_bounds__(448, 1)
       fence_proxy_async_smem();
       mbar_arrive(bar(BB_SM + h));
       if (tt == T_h - 1) {  // end of q-head g: each warp writes its dn/db partial
-        float x1 = dn_acc, x2 = db_acc;
+        float x1 = (dn_acc[0] + dn_acc[1]) + (dn_acc[2] + dn_acc[3]);
+        float x2 = (db_acc[0] + db_acc[1]) + (db_acc[2] + db_acc[3]);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
           x1 += __shfl_xor_sync(0xffffffffu, x1, o);
@@ -420,8 +453,8 @@ __global__ void __launch_bounds__(448, 1)
           a.dn_part[pi] = x1 * kLn2;
           a.db_part[pi] = x2 * n * p.scale;
         }
-        dn_acc = 0.f;
-        db_acc = 0.f;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) dn_acc[i] = db_acc[i] = 0.f;
       }
     }
     if (!ok) *abort_flag = 1;
@@ -450,14 +483,14 @@ __global__ void __launch_bounds__(448, 1)
       }
     }
   } else {
-    // ---------------------------------------------------------------- dQ drain (warps 10..13)
-    // Each warp drains its own 32 query rows: TMEM -> its 8 KB of the staging buffer -> one
-    // bulk reduce-add of 8 KB (the 32 rows are contiguous in the dQ accumulator).
+    // ---------------------------------------------------------------- dQ drain (warps 8..11)
+    regs_dec<C::REGS_DQ>();
+    // Each warp drains its own 32 query rows in two 32-column halves: TMEM -> 4 KB of staging in
+    // the 128-byte swizzle -> one 2-D TMA reduce-add (fp32) per half into the dQ accumulator.
     const int quad = warp & 3;
-    const int r = quad * 32 + lane;  // query row within the tile
+    uint8_t* stage = smem + C::OFF_DQS + quad * C::DQS_WARP;
+    const uint32_t stage_s = sbase + C::OFF_DQS + quad * C::DQS_WARP;
     const uint32_t tQ = tmem + ((uint32_t)(quad * 32) << 16) + C::COL_DQ;
-    float* stage = reinterpret_cast<float*>(smem + C::OFF_DQS) + quad * 32 * C::D;
-    const uint32_t stage_s = sbase + C::OFF_DQS + quad * 32 * C::D * 4;
     bool ok = true;
     for (int t = 0; t < T; ++t) {
       ok = mbar_wait(bar(BB_DQF), t & 1, a.status);
@@ -475,34 +508,36 @@ __global__ void __launch_bounds__(448, 1)
       tmem_pin(v1);
       tc_fence_before();
       mbar_arrive(bar(BB_DQE));
-      if (lane == 0) bulk_wait_read0();  // this warp's staging rows are free again
-      __syncwarp();
-      uint4* srow = reinterpret_cast<uint4*>(stage + lane * C::D);
+      const int g = t / T_h, tt = t - g * T_h;
+      const int hq = hkv * p.gqa + g;
+      const int m0 = q_start + tt * C::BT + quad * 32;
+      const int row0 = p.cu_seqlens ? (int)((int64_t)hq * a.dq_rows + seq_start + m0)
+                                    : (int)(((int64_t)z * p.Hq + hq) * a.dq_rows + m0);
 #pragma unroll
-      for (int i = 0; i < 8; ++i) srow[i] = make_uint4(v0[4 * i], v0[4 * i + 1], v0[4 * i + 2], v0[4 * i + 3]);
+      for (int hc = 0; hc < 2; ++hc) {
+        const uint32_t(&v)[32] = hc ? v1 : v0;
+        if (lane == 0) bulk_wait_read0();  // the staging buffer is free again
+        __syncwarp();
+        uint8_t* srow = stage + lane * 128;
 #pragma unroll
-      for (int i = 0; i < 8; ++i)
-        srow[8 + i] = make_uint4(v1[4 * i], v1[4 * i + 1], v1[4 * i + 2], v1[4 * i + 3]);
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) {
-        const int g = t / T_h, tt = t - g * T_h;
-        const int hq = hkv * p.gqa + g;
-        const int m0 = q_start + tt * C::BT + quad * 32;
-        const int64_t row0 = p.cu_seqlens ? (int64_t)hq * a.dq_rows + seq_start + m0
-                                          : ((int64_t)z * p.Hq + hq) * a.dq_rows + m0;
-        bulk_reduce_add_f32(a.dq_accum + row0 * C::D, stage_s, 32 * C::D * 4);
-        bulk_commit();
+        for (int i = 0; i < 8; ++i)
+          *reinterpret_cast<uint4*>(srow + ((i ^ (lane & 7)) << 4)) =
+              make_uint4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_reduce_add_2d(&tmDQ, stage_s, hc * 32, row0);
+          bulk_commit();
+        }
       }
     }
     if (!ok) *abort_flag = 1;
     if (lane == 0) bulk_wait0();
-    (void)r;
   }
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 0) {
+  if (warp == C::WARP_PRODUCER) {
     __syncwarp();
     tc_fence_after();
     tmem_dealloc(tmem, C::TMEM_COLS);
@@ -586,12 +621,28 @@ int run_bwd(const Problem& p, TensorRef q, TensorRef k, TensorRef v, TensorRef d
   a.status = device_status_ptr();
   a.nkv = lay.nkv;
   if (cudaMemsetAsync(a.dq_accum, 0, lay.dq_bytes, st) != cudaSuccess) return SSA_ERR_CUDA;
+  // dQ accumulator as a 2-D fp32 tensor [rows][64] for the drain's tiled reduce-adds:
+  // {32 columns x 32 rows} boxes in the 128-byte swizzle.
+  CUtensorMap tdq;
+  {
+    auto enc = tmap_encoder();
+    if (!enc) return SSA_ERR_CUDA;
+    const uint64_t rows = (uint64_t)(p.cu_seqlens ? p.Hq : p.B * p.Hq) * (uint64_t)lay.dq_rows;
+    cuuint64_t dims[2] = {(cuuint64_t)C::D, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)C::D * 4};
+    cuuint32_t box[2] = {32u, 32u};
+    cuuint32_t estr[2] = {1u, 1u};
+    if (enc(&tdq, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, a.dq_accum, dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return SSA_ERR_CUDA;
+  }
   auto kern = bwd_sm100_kernel<BF16>;
   if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                            (int)C::SMEM_BYTES) != cudaSuccess)
     return SSA_ERR_CUDA;
   const long long grid = (long long)lay.nkv * p.B * p.Hkv;
-  kern<<<(unsigned)grid, C::THREADS, C::SMEM_BYTES, st>>>(tq, tk, tv, tdo, a);
+  kern<<<(unsigned)grid, C::THREADS, C::SMEM_BYTES, st>>>(tq, tk, tv, tdo, tdq, a);
   using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
   dim3 gc((p.max_seqlen + 31) / 32, p.B * p.Hq);
   dq_convert_kernel<T><<<gc, 256, 0, st>>>(p, a.dq_accum, a.dq_rows, dq);

@@ -15,7 +15,8 @@
 //               lse / delta rows into shared memory with plain loads.
 //   warp 13     MMA issuer (tcgen05, fp32 accumulation in TMEM):
 //                 S^T  = K Q_h^T,  dP^T = V dO_h^T          (SS, M=128 keys, N=64 queries)
-//                 dV  += P^T dO_h,  dK += dS^T Q_h          (TS: P^T / dS^T read from TMEM)
+//                 dV  += P^T dO_h                           (TS: P^T read from TMEM)
+//                 dK  += dS^T Q_h                           (SS: dS^T from shared memory)
 //                 dQ   = dS K                               (SS, M=128 queries, dS from smem)
 //   warps 0..3  half 0 of each tile, one thread per key row: SSA transform, P, dS, dn/db
 //   warps 4..7  half 1 of each tile
@@ -23,8 +24,9 @@
 //               dQ accumulator in global memory; a small kernel converts it to dq's dtype.
 // The roles sit on whole warpgroups so setmaxnreg can move registers to the P/dS groups.
 // TMEM (512 columns): S/dP for half 0 [0,128), for half 1 [128,256), dK [256,320),
-// dV [320,384), dQ [384,448). P^T and dS^T (packed 16-bit) overwrite the S and dP columns
-// they were computed from.
+// dV [320,384), dQ [384,448), P^T (packed 16-bit) of half h at [448 + 32h, 480 + 32h). With
+// P^T outside the S/dP buffers and dS^T in shared memory, the next tile's S^T/dP^T MMAs can be
+// issued right behind the grads MMAs without waiting for them to retire.
 //
 // dn / db: per-thread fp32 sums, reduced per warp at the end of each q-head and written as
 // partials [z][hq][key block][half][warp]; a deterministic fp64 kernel sums them.
@@ -66,14 +68,15 @@ struct BwdCfg {
   static constexpr uint32_t TMEM_COLS = 512;
   static constexpr uint32_t COL_S0 = 0, COL_DP0 = 64, COL_S1 = 128, COL_DP1 = 192;
   static constexpr uint32_t COL_DK = 256, COL_DV = 320, COL_DQ = 384;
+  static constexpr uint32_t COL_PT = 448;  // P^T (packed 16-bit) for half h at COL_PT + 32 h
   static constexpr int THREADS = 512;
   // Warp roles (warpgroup-aligned so each group can resize its register file):
   //   warps 0..3 / 4..7  P/dS for query halves 0 / 1   (regs raised to REGS_PDS)
   //   warps 8..11        dQ drain                       (REGS_DQ)
   //   warp 12 TMA producer, warp 13 MMA issuer, 14..15 idle (REGS_CTRL)
-  // Budget at launch: 512 threads x 128 = 65536; after the moves 2*128*184 + 128*88 + 128*56
+  // Budget at launch: 512 threads x 128 = 65536; after the moves 2*128*176 + 128*88 + 128*72
   // = 65536.
-  static constexpr uint32_t REGS_PDS = 184, REGS_DQ = 88, REGS_CTRL = 56;
+  static constexpr uint32_t REGS_PDS = 176, REGS_DQ = 88, REGS_CTRL = 72;
   static constexpr int WARP_PRODUCER = 12, WARP_MMA = 13;
 };
 static_assert(BwdCfg::SMEM_BYTES <= 232448, "shared memory budget");
@@ -288,11 +291,17 @@ __global__ void __launch_bounds__(512, 1)
     }
    } else if (warp == C::WARP_MMA) {
     // ---------------------------------------------------------------- MMA issuer
-    if (lane == 0) {
+    // The whole warp runs the schedule (waits, descriptor arithmetic); one elected lane issues
+    // each tcgen05.mma / commit through a predicate.
+    {
+      const uint32_t leader = elect_one();
       constexpr uint32_t id_s = idesc_f16(BF16, false, false, 128, 64);  // S^T, dP^T
       constexpr uint32_t id_g = idesc_f16(BF16, false, true, 128, 64);   // dV, dK
       constexpr uint32_t id_q = idesc_f16(BF16, true, true, 128, 64);    // dQ
       const uint32_t sK = sbase + C::OFF_K, sV = sbase + C::OFF_V;
+      auto wait_all = [&](uint32_t b, uint32_t par) {
+        return __all_sync(0xffffffffu, mbar_wait(b, par, a.status));
+      };
       auto issue_sdp = [&](int t, int h) {
         const int st = t % C::STAGES;
         const uint32_t qb = sbase + C::OFF_Q + st * C::QT_BYTES + h * C::HALF_BYTES;
@@ -300,15 +309,15 @@ __global__ void __launch_bounds__(512, 1)
         const uint32_t cs = h ? C::COL_S1 : C::COL_S0, cdp = h ? C::COL_DP1 : C::COL_DP0;
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
-          mma_ss(tmem + cs, sdesc_sw128(sK + kk * 32, 16, 1024), sdesc_sw128(qb + kk * 32, 16, 1024),
-                 id_s, kk > 0 ? 1u : 0u);
+          mma_ss_p(tmem + cs, sdesc_sw128(sK + kk * 32, 16, 1024),
+                   sdesc_sw128(qb + kk * 32, 16, 1024), id_s, kk > 0 ? 1u : 0u, leader);
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)
-          mma_ss(tmem + cdp, sdesc_sw128(sV + kk * 32, 16, 1024),
-                 sdesc_sw128(db + kk * 32, 16, 1024), id_s, kk > 0 ? 1u : 0u);
-        mma_commit(bar(BB_SF + h));
+          mma_ss_p(tmem + cdp, sdesc_sw128(sV + kk * 32, 16, 1024),
+                   sdesc_sw128(db + kk * 32, 16, 1024), id_s, kk > 0 ? 1u : 0u, leader);
+        mma_commit_p(bar(BB_SF + h), leader);
       };
-      bool ok = mbar_wait(bar(BB_KV), 0, a.status) && mbar_wait(bar(BB_QF), 0, a.status);
+      bool ok = wait_all(bar(BB_KV), 0) && wait_all(bar(BB_QF), 0);
       if (ok) {
         tc_fence_after();
         issue_sdp(0, 0);
@@ -317,46 +326,50 @@ __global__ void __launch_bounds__(512, 1)
       for (int t = 0; ok && t < T; ++t) {
         const int st = t % C::STAGES, dsb = t & 1;
         for (int h = 0; h < 2 && ok; ++h) {
-          ok = mbar_wait(bar(BB_SM + h), t & 1, a.status);
+          ok = wait_all(bar(BB_SM + h), t & 1);
           if (!ok || *abort_flag) break;
           tc_fence_after();
           const uint32_t qb = sbase + C::OFF_Q + st * C::QT_BYTES + h * C::HALF_BYTES;
           const uint32_t db = sbase + C::OFF_DO + st * C::QT_BYTES + h * C::HALF_BYTES;
-          const uint32_t cs = h ? C::COL_S1 : C::COL_S0, cdp = h ? C::COL_DP1 : C::COL_DP0;
+          const uint32_t dsh = sbase + C::OFF_DS + dsb * C::DS_BYTES + h * C::DS_SLAB;
+          // dV += P^T dO_h (P^T from TMEM); dK += dS^T Q_h (dS^T from the shared slab the dQ
+          // MMA also reads: [128 keys x 64 queries], K-major here, MN-major for dQ).
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            mma_ts(tmem + C::COL_DV, tmem + cs + kk * 8, sdesc_sw128(db + kk * 2048, 8192, 1024),
-                   id_g, (t > 0 || h > 0 || kk > 0) ? 1u : 0u);
+            mma_ts_p(tmem + C::COL_DV, tmem + C::COL_PT + h * 32 + kk * 8,
+                     sdesc_sw128(db + kk * 2048, 8192, 1024), id_g,
+                     (t > 0 || h > 0 || kk > 0) ? 1u : 0u, leader);
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
-            mma_ts(tmem + C::COL_DK, tmem + cdp + kk * 8, sdesc_sw128(qb + kk * 2048, 8192, 1024),
-                   id_g, (t > 0 || h > 0 || kk > 0) ? 1u : 0u);
-          mma_commit(bar(BB_BF + h));
+            mma_ss_p(tmem + C::COL_DK, sdesc_sw128(dsh + kk * 32, 16, 1024),
+                     sdesc_sw128(qb + kk * 2048, 8192, 1024), id_g,
+                     (t > 0 || h > 0 || kk > 0) ? 1u : 0u, leader);
+          mma_commit_p(bar(BB_BF + h), leader);
+          // S^T / dP^T of the next tile may overwrite this half's buffer at once: the P/dS
+          // group has already read it, and grads no longer read it.
           if (t + 1 < T) {
-            if (h == 0)
-              ok = mbar_wait(bar(BB_QF + (t + 1) % C::STAGES), ((t + 1) / C::STAGES) & 1, a.status);
-            if (ok) ok = mbar_wait(bar(BB_BF + h), t & 1, a.status);  // P^T/dS^T consumed
+            if (h == 0) ok = wait_all(bar(BB_QF + (t + 1) % C::STAGES), ((t + 1) / C::STAGES) & 1);
             if (!ok) break;
             tc_fence_after();
             issue_sdp(t + 1, h);
           }
         }
         if (!ok || *abort_flag) break;
-        if (t >= 1) ok = mbar_wait(bar(BB_DQE), (t - 1) & 1, a.status);
+        if (t >= 1) ok = wait_all(bar(BB_DQE), (t - 1) & 1);
         if (!ok) break;
         tc_fence_after();
         const uint32_t ds = sbase + C::OFF_DS + dsb * C::DS_BYTES;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
-          mma_ss(tmem + C::COL_DQ, sdesc_sw128(ds + kk * 2048, C::DS_SLAB, 1024),
-                 sdesc_sw128(sK + kk * 2048, 8192, 1024), id_q, kk > 0 ? 1u : 0u);
-        mma_commit(bar(BB_DQF));
-        mma_commit(bar(BB_DSF + dsb));
-        mma_commit(bar(BB_QE + st));
+          mma_ss_p(tmem + C::COL_DQ, sdesc_sw128(ds + kk * 2048, C::DS_SLAB, 1024),
+                   sdesc_sw128(sK + kk * 2048, 8192, 1024), id_q, kk > 0 ? 1u : 0u, leader);
+        mma_commit_p(bar(BB_DQF), leader);
+        mma_commit_p(bar(BB_DSF + dsb), leader);
+        mma_commit_p(bar(BB_QE + st), leader);
       }
       if (!ok) *abort_flag = 1;
-      mma_commit(bar(BB_KVD));
-      mma_commit(bar(BB_END));
+      mma_commit_p(bar(BB_KVD), leader);
+      mma_commit_p(bar(BB_END), leader);
       mbar_wait(bar(BB_END), 0, a.status);
     }
    }
@@ -370,6 +383,7 @@ __global__ void __launch_bounds__(512, 1)
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
     const uint32_t tS = tmem + lane_off + (h ? C::COL_S1 : C::COL_S0);
     const uint32_t tP = tmem + lane_off + (h ? C::COL_DP1 : C::COL_DP0);
+    const uint32_t tPT = tmem + lane_off + C::COL_PT + h * 32;
     const float bval = __ldg(p.b_ptr);
     const float cb = bval * p.scale;
     float n = 0.f, nbs = 0.f;
@@ -420,14 +434,16 @@ __global__ void __launch_bounds__(512, 1)
         else
           bwd_chunk<32, BF16, true>(cs, cd, lrow + c * 32, drow + c * 32, n, cb, nbs, mh + c * 32,
                                     qmin, L, j < L, dn_acc, db_acc, pk, dk);
-        if (c == 0) {  // chunk 1 must be in registers before columns [0, 16) are overwritten
+        if (c == 0) {
           tmem_ld_wait_only();
           tmem_pin_n(sxb);
           tmem_pin_n(dpb);
+          // dV(t-1) must have read this half's P^T columns before they are rewritten.
+          bool okb = t == 0 || mbar_wait(bar(BB_BF + h), (t - 1) & 1, a.status);
+          if (!__all_sync(0xffffffffu, okb)) *abort_flag = 1;
+          tc_fence_after();
         }
-        // P^T / dS^T (packed) overwrite columns [16c, 16c+16), already loaded.
-        tmem_st16(tS + c * 16, pk);
-        tmem_st16(tP + c * 16, dk);
+        tmem_st16(tPT + c * 16, pk);
         // dS^T row r of this half's slab: 16-byte chunks, 128-byte swizzle (chunk ^ (row & 7))
 #pragma unroll
         for (int q4 = 0; q4 < 4; ++q4) {

@@ -171,15 +171,20 @@ __global__ void __launch_bounds__(192, 2)
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
+    // The whole warp runs the schedule; one elected lane issues each tcgen05.mma / commit.
+    {
+      const uint32_t leader = elect_one();
       constexpr uint32_t idesc_s = idesc_f16(BF16, false, false, 128, C::BN);
       constexpr uint32_t idesc_o = idesc_f16(BF16, false, true, 128, D);
-      bool ok = mbar_wait(bar(FB_Q), 0, a.status);
+      auto wait_all = [&](uint32_t b, uint32_t par) {
+        return __all_sync(0xffffffffu, mbar_wait(b, par, a.status));
+      };
+      bool ok = wait_all(bar(FB_Q), 0);
       for (int j = 0; ok && j < nblk; ++j) {
         const int st = j & 1, u = j >> 1;
-        ok = mbar_wait(bar(FB_KF + st), u & 1, a.status);
+        ok = wait_all(bar(FB_KF + st), u & 1);
         // S/P columns are reused: the previous P V must have finished reading P.
-        if (ok && j > 0) ok = mbar_wait(bar(FB_O), (j - 1) & 1, a.status);
+        if (ok && j > 0) ok = wait_all(bar(FB_O), (j - 1) & 1);
         if (!ok || *abort_flag) break;
         tc_fence_after();
 #pragma unroll
@@ -189,25 +194,25 @@ __global__ void __launch_bounds__(192, 2)
           const uint64_t ad = sdesc_sw128(sbase + C::OFF_Q + slab * C::BM * 128 + off, 16, 1024);
           const uint64_t bd = sdesc_sw128(
               sbase + C::OFF_K + st * C::KV_BYTES + slab * C::BN * 128 + off, 16, 1024);
-          mma_ss(tmem + C::COL_S, ad, bd, idesc_s, kk > 0 ? 1u : 0u);
+          mma_ss_p(tmem + C::COL_S, ad, bd, idesc_s, kk > 0 ? 1u : 0u, leader);
         }
-        mma_commit(bar(FB_S));
-        ok = mbar_wait(bar(FB_VF + st), u & 1, a.status);
-        if (ok) ok = mbar_wait(bar(FB_P), j & 1, a.status);
+        mma_commit_p(bar(FB_S), leader);
+        ok = wait_all(bar(FB_VF + st), u & 1);
+        if (ok) ok = wait_all(bar(FB_P), j & 1);
         if (!ok || *abort_flag) break;
         tc_fence_after();
 #pragma unroll
         for (int kk = 0; kk < C::BN / 16; ++kk) {
           const uint64_t bd = sdesc_sw128(sbase + C::OFF_V + st * C::KV_BYTES + kk * 16 * 128,
                                           C::BN * 128, 1024);
-          mma_ts(tmem + C::COL_O, tmem + C::COL_S + kk * 8, bd, idesc_o,
-                 (j > 0 || kk > 0) ? 1u : 0u);
+          mma_ts_p(tmem + C::COL_O, tmem + C::COL_S + kk * 8, bd, idesc_o,
+                   (j > 0 || kk > 0) ? 1u : 0u, leader);
         }
-        mma_commit(bar(FB_O));
-        mma_commit(bar(FB_KVE + st));
+        mma_commit_p(bar(FB_O), leader);
+        mma_commit_p(bar(FB_KVE + st), leader);
       }
       if (!ok) *abort_flag = 1;
-      mma_commit(bar(FB_END));  // all MMAs of this CTA retired before TMEM is freed
+      mma_commit_p(bar(FB_END), leader);  // all MMAs of this CTA retired before TMEM is freed
       mbar_wait(bar(FB_END), 0, a.status);
     }
   } else {

@@ -329,6 +329,13 @@ __global__ void __launch_bounds__(512, 1)
           ok = wait_all(bar(BB_SM + h), t & 1);
           if (!ok || *abort_flag) break;
           tc_fence_after();
+          // The next tile's S^T / dP^T go first: this half's buffer has been read by the P/dS
+          // group, and the grads below read only P^T (own TMEM columns) and dS^T (shared).
+          if (t + 1 < T) {
+            if (h == 0) ok = wait_all(bar(BB_QF + (t + 1) % C::STAGES), ((t + 1) / C::STAGES) & 1);
+            if (!ok) break;
+            issue_sdp(t + 1, h);
+          }
           const uint32_t qb = sbase + C::OFF_Q + st * C::QT_BYTES + h * C::HALF_BYTES;
           const uint32_t db = sbase + C::OFF_DO + st * C::QT_BYTES + h * C::HALF_BYTES;
           const uint32_t dsh = sbase + C::OFF_DS + dsb * C::DS_BYTES + h * C::DS_SLAB;
@@ -345,14 +352,6 @@ __global__ void __launch_bounds__(512, 1)
                      sdesc_sw128(qb + kk * 2048, 8192, 1024), id_g,
                      (t > 0 || h > 0 || kk > 0) ? 1u : 0u, leader);
           mma_commit_p(bar(BB_BF + h), leader);
-          // S^T / dP^T of the next tile may overwrite this half's buffer at once: the P/dS
-          // group has already read it, and grads no longer read it.
-          if (t + 1 < T) {
-            if (h == 0) ok = wait_all(bar(BB_QF + (t + 1) % C::STAGES), ((t + 1) / C::STAGES) & 1);
-            if (!ok) break;
-            tc_fence_after();
-            issue_sdp(t + 1, h);
-          }
         }
         if (!ok || *abort_flag) break;
         if (t >= 1) ok = wait_all(bar(BB_DQE), (t - 1) & 1);
@@ -412,32 +411,27 @@ __global__ void __launch_bounds__(512, 1)
       const float* drow = del_s + st * C::BT + h * 64;
       uint8_t* dsrow = smem + C::OFF_DS + dsb * C::DS_BYTES + h * C::DS_SLAB + r * 128;
       const int qmin = p.causal ? j : 0;
-      // 2 chunks of 32 queries; chunk 1's S / dP loads are in flight while chunk 0 computes.
-      uint32_t sxa[32], dpa[32], sxb[32], dpb[32];
-      tmem_ld32(tS, sxa);
-      tmem_ld32(tP, dpa);
+      // 2 chunks of 32 queries. Chunk 1's S / dP loads are issued after chunk 0 has been
+      // computed (so chunk 0 keeps every register for instruction-level parallelism) and are in
+      // flight while chunk 0's P^T and dS^T are stored.
+      uint32_t sx[32], dp[32];
+      tmem_ld32(tS, sx);
+      tmem_ld32(tP, dp);
       tmem_ld_wait_only();
-      tmem_pin_n(sxa);
-      tmem_pin_n(dpa);
+      tmem_pin_n(sx);
+      tmem_pin_n(dp);
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
-        uint32_t(&cs)[32] = c ? sxb : sxa;
-        uint32_t(&cd)[32] = c ? dpb : dpa;
-        if (c == 0) {
-          tmem_ld32(tS + 32, sxb);
-          tmem_ld32(tP + 32, dpb);
-        }
         uint32_t pk[16], dk[16];
         if (full)
-          bwd_chunk<32, BF16, false>(cs, cd, lrow + c * 32, drow + c * 32, n, cb, nbs, mh + c * 32,
+          bwd_chunk<32, BF16, false>(sx, dp, lrow + c * 32, drow + c * 32, n, cb, nbs, mh + c * 32,
                                      qmin, L, j < L, dn_acc, db_acc, pk, dk);
         else
-          bwd_chunk<32, BF16, true>(cs, cd, lrow + c * 32, drow + c * 32, n, cb, nbs, mh + c * 32,
+          bwd_chunk<32, BF16, true>(sx, dp, lrow + c * 32, drow + c * 32, n, cb, nbs, mh + c * 32,
                                     qmin, L, j < L, dn_acc, db_acc, pk, dk);
         if (c == 0) {
-          tmem_ld_wait_only();
-          tmem_pin_n(sxb);
-          tmem_pin_n(dpb);
+          tmem_ld32(tS + 32, sx);
+          tmem_ld32(tP + 32, dp);
           // dV(t-1) must have read this half's P^T columns before they are rewritten.
           bool okb = t == 0 || mbar_wait(bar(BB_BF + h), (t - 1) & 1, a.status);
           if (!__all_sync(0xffffffffu, okb)) *abort_flag = 1;
@@ -450,6 +444,11 @@ __global__ void __launch_bounds__(512, 1)
           const int chunk = c * 4 + q4;
           *reinterpret_cast<uint4*>(dsrow + ((chunk ^ (r & 7)) << 4)) =
               make_uint4(dk[q4 * 4], dk[q4 * 4 + 1], dk[q4 * 4 + 2], dk[q4 * 4 + 3]);
+        }
+        if (c == 0) {
+          tmem_ld_wait_only();
+          tmem_pin_n(sx);
+          tmem_pin_n(dp);
         }
       }
       tmem_st_wait();

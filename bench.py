@@ -21,8 +21,9 @@ Lines printed (rank 0, one JSON line):
   roofline  the backward call (the dominant launch) against the measured dense bf16 peak;
   cpu_baseline  the CPU oracle (fp32 eager restatement of the reference's SSA math) timed on
             this host's cores on a bounded sample (one q-head of one sequence).
-``--impl reference`` times that CPU restatement alone (the reference's own code cannot run on
-the GPU box) and prints its line with "impl": "reference".
+``--impl reference`` times that CPU restatement alone (the reference's own Triton code is not
+present on the GPU box and may not be copied into this repository) and prints its line with
+"impl": "reference".
 """
 
 from __future__ import annotations
@@ -51,9 +52,9 @@ WORKLOAD = "config2: SSA causal GQA fwd+bwd, B=8 Hq=32 Hkv=8 S=2048 D=64 bf16, p
 METRIC = "SSA attn fwd+bwd TFLOP/s (bf16, B=8 Hq=32 Hkv=8 S=2048 D=64 causal)"
 UNIT = "TFLOP/s"
 
-# ncu DRAM traffic (read+write bytes) per launch of the dominant kernel, from the capture
-# summarised in profiles/ (None until captured for the current kernel).
-NCU_TRAFFIC_BYTES = None
+# ncu DRAM traffic (read+write bytes) per launch of the dominant kernel (bwd_sm100_kernel),
+# taken from one ncu capture of this workload; None when no capture matches the current kernel.
+NCU_TRAFFIC_BYTES = 1.518e9  # bwd_sm100_kernel, one ncu capture at config 2: dram read + write
 
 
 def flops_per_rank() -> float:
@@ -229,6 +230,7 @@ def main():
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     from SSA import _lib
+    from SSA.shard import allreduce_ssa_param_grads
     from SSA.ssa_triton_kernel import ssa_flash_attn_backward, ssa_flash_attn_forward
     import torch.distributed as dist
 
@@ -243,9 +245,7 @@ def main():
         out, m = ssa_flash_attn_forward(q, k, v, scale, n, bb, causal=CAUSAL)
         dq, dk, dv, dn, db = ssa_flash_attn_backward(q, k, v, out, do, m, scale, n, bb, causal=CAUSAL)
         if world > 1:
-            red[:HQ].copy_(dn)
-            red[HQ:].copy_(db.reshape(1))
-            dist.all_reduce(red)
+            allreduce_ssa_param_grads(dn, db, buffer=red)
         return out, dq, dk, dv, dn, db
 
     def barrier():
@@ -275,9 +275,7 @@ def main():
                                                          causal=CAUSAL)
             e2.record(st)
             if world > 1:
-                red[:HQ].copy_(dn)
-                red[HQ:].copy_(db.reshape(1))
-                dist.all_reduce(red)
+                allreduce_ssa_param_grads(dn, db, buffer=red)
         stop.record(st)
         barrier()
     launches = _lib.launch_count() - launches0
@@ -304,10 +302,10 @@ def main():
         out_, m_ = ssa_flash_attn_forward(qd, kd, vd, scale, n, bb, causal=CAUSAL)
         dq_, dk_, dv_, dn_, db_ = ssa_flash_attn_backward(qd, kd, vd, out_, dod, m_, scale, n, bb,
                                                           causal=CAUSAL)
+        if world > 1:
+            allreduce_ssa_param_grads(dn_, db_, buffer=red)
         red[:HQ].copy_(dn_)
         red[HQ:].copy_(db_.reshape(1))
-        if world > 1:
-            dist.all_reduce(red)
         for dst, src in zip(outs_p, (out_, dq_, dk_, dv_, red)):
             dst.copy_(src, non_blocking=True)
 

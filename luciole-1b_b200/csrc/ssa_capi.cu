@@ -279,8 +279,6 @@ int ssa_attn_bwd(const ssa_problem_t* prob, ssa_tensor_t q, ssa_tensor_t k, ssa_
   const BwdWorkspace w = carve_bwd(prob, workspace);
   const Problem p = to_problem(prob);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  rc = launch_bwd_preprocess(prob->dtype, p, to_ref(out), to_ref(dout), w.delta, st);
-  if ((rc = finish_launch(rc, "ssa_attn_bwd(preprocess)")) != SSA_OK) return rc;
   if (use_sm100_bwd(prob)) {
     if ((rc = check_tma(p, q, p.Hq, "q")) || (rc = check_tma(p, k, p.Hkv, "k")) ||
         (rc = check_tma(p, v, p.Hkv, "v")) || (rc = check_tma(p, dout, p.Hq, "dout")) ||
@@ -288,11 +286,17 @@ int ssa_attn_bwd(const ssa_problem_t* prob, ssa_tensor_t q, ssa_tensor_t k, ssa_
         (rc = check_tma(p, dv, p.Hkv, "dv")))
       return rc;
     if (!device_status_ptr()) return fail(SSA_ERR_CUDA, "cannot resolve the device status word");
+    if ((reinterpret_cast<uintptr_t>(out.ptr) % 16) || (out.sN * 2) % 16 || (out.sH * 2) % 16 ||
+        (out.sB * 2) % 16)
+      return fail(SSA_ERR_BAD_STRIDE, "out: base and strides must be 16-byte aligned");
     return finish_launch(launch_bwd_sm100(prob->dtype, p, to_ref(q), to_ref(k), to_ref(v),
-                                          to_ref(dout), lse, w.delta, to_ref(dq), to_ref(dk),
-                                          to_ref(dv), dn, db, w.sm100, w.sm100_bytes, st),
+                                          to_ref(out), to_ref(dout), lse, w.delta, to_ref(dq),
+                                          to_ref(dk), to_ref(dv), dn, db, w.sm100, w.sm100_bytes,
+                                          st),
                          "ssa_attn_bwd(sm100)");
   }
+  rc = launch_bwd_preprocess(prob->dtype, p, to_ref(out), to_ref(dout), w.delta, st);
+  if ((rc = finish_launch(rc, "ssa_attn_bwd(preprocess)")) != SSA_OK) return rc;
   rc = launch_bwd_generic(prob->dtype, p, to_ref(q), to_ref(k), to_ref(v), to_ref(dout), lse,
                           w.delta, to_ref(dq), to_ref(dk), to_ref(dv), w.dn_part, w.db_part, st);
   if ((rc = finish_launch(rc, "ssa_attn_bwd(generic)")) != SSA_OK) return rc;

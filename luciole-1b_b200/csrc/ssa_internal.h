@@ -25,8 +25,9 @@ int launch_fwd_sm100(int dtype, const Problem& p, TensorRef q, TensorRef k, Tens
                      TensorRef o, float* lse, cudaStream_t st);
 bool sm100_bwd_supports(int dtype, int D);
 size_t sm100_bwd_workspace_bytes(const Problem& p);
+// Runs its own fused preprocess (delta + dQ-accumulator zeroing) before the main kernel.
 int launch_bwd_sm100(int dtype, const Problem& p, TensorRef q, TensorRef k, TensorRef v,
-                     TensorRef dout, const float* lse, const float* delta, TensorRef dq,
+                     TensorRef out, TensorRef dout, const float* lse, float* delta, TensorRef dq,
                      TensorRef dk, TensorRef dv, float* dn, float* db, void* ws, size_t ws_bytes,
                      cudaStream_t st);
 

@@ -559,6 +559,55 @@ __global__ void __launch_bounds__(512, 1)
   }
 }
 
+// Backward preprocess for the tensor-core path, one pass: delta = rowsum(O * dO) in fp32
+// (ssa_triton_kernel.py:267-298) and zeroing of the fp32 dQ accumulator rows (padding rows
+// included). 8 threads per row, 16-byte loads; 32 rows per 256-thread block.
+template <typename T>
+__global__ void __launch_bounds__(256) bwd_preprocess_sm100_kernel(Problem p, TensorRef o,
+                                                                   TensorRef dout, float* delta,
+                                                                   float* dq_accum,
+                                                                   int64_t dq_rows) {
+  const int sub = threadIdx.x & 7;
+  const int rr = blockIdx.x * 32 + (threadIdx.x >> 3);  // row within the head's accumulator
+  if (rr >= dq_rows) return;
+  int z, hq, row, L;
+  if (p.cu_seqlens) {  // accumulator rows are packed tokens; delta is [Hq][T]
+    z = 0;
+    hq = blockIdx.y;
+    row = rr;
+    L = p.N;
+  } else {
+    z = blockIdx.y / p.Hq;
+    hq = blockIdx.y % p.Hq;
+    row = rr;
+    L = p.N;
+  }
+  float4* zdst = reinterpret_cast<float4*>(
+      dq_accum + ((int64_t)blockIdx.y * dq_rows + rr) * 64 + sub * 8);
+  zdst[0] = make_float4(0.f, 0.f, 0.f, 0.f);
+  zdst[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+  float acc = 0.f;
+  const bool valid = row < L;
+  if (valid) {
+    const int64_t oo = (p.cu_seqlens ? 0 : (int64_t)z * o.sB) + (int64_t)hq * o.sH + (int64_t)row * o.sN;
+    const int64_t od = (p.cu_seqlens ? 0 : (int64_t)z * dout.sB) + (int64_t)hq * dout.sH +
+                       (int64_t)row * dout.sN;
+    const uint4 a = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(o.ptr) + oo + sub * 8);
+    const uint4 b = *reinterpret_cast<const uint4*>(reinterpret_cast<const T*>(dout.ptr) + od + sub * 8);
+    const T* ae = reinterpret_cast<const T*>(&a);
+    const T* be = reinterpret_cast<const T*>(&b);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc = fmaf(to_f32<T>(ae[i]), to_f32<T>(be[i]), acc);
+  }
+  acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+  acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+  acc += __shfl_xor_sync(0xffffffffu, acc, 4);
+  if (valid && sub == 0) {
+    const int64_t so = p.cu_seqlens ? (int64_t)hq * p.N + row : ((int64_t)z * p.Hq + hq) * p.N + row;
+    delta[so] = acc;
+  }
+}
+
 // dq (q's dtype, caller strides) = dq_accum (fp32) for the valid rows.
 template <typename T>
 __global__ void __launch_bounds__(256) dq_convert_kernel(Problem p, const float* dq_accum,
@@ -609,9 +658,9 @@ BwdLayout bwd_layout(const Problem& p) {
 }
 
 template <bool BF16>
-int run_bwd(const Problem& p, TensorRef q, TensorRef k, TensorRef v, TensorRef dout,
-            const float* lse, const float* delta, TensorRef dq, TensorRef dk, TensorRef dv,
-            float* dn, float* db, void* ws, size_t ws_bytes, cudaStream_t st) {
+int run_bwd(const Problem& p, TensorRef q, TensorRef k, TensorRef v, TensorRef out,
+            TensorRef dout, const float* lse, float* delta, TensorRef dq, TensorRef dk,
+            TensorRef dv, float* dn, float* db, void* ws, size_t ws_bytes, cudaStream_t st) {
   using C = BwdCfg;
   const int dtype = BF16 ? SSA_DTYPE_BF16 : SSA_DTYPE_F16;
   const BwdLayout lay = bwd_layout(p);
@@ -635,7 +684,13 @@ int run_bwd(const Problem& p, TensorRef q, TensorRef k, TensorRef v, TensorRef d
   a.db_part = reinterpret_cast<float*>(w + lay.dq_bytes + lay.part_bytes);
   a.status = device_status_ptr();
   a.nkv = lay.nkv;
-  if (cudaMemsetAsync(a.dq_accum, 0, lay.dq_bytes, st) != cudaSuccess) return SSA_ERR_CUDA;
+  {
+    using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+    dim3 gp((unsigned)((lay.dq_rows + 31) / 32), p.cu_seqlens ? p.Hq : p.B * p.Hq);
+    bwd_preprocess_sm100_kernel<T><<<gp, 256, 0, st>>>(p, out, dout, delta, a.dq_accum,
+                                                        lay.dq_rows);
+    note_launches(1);
+  }
   // dQ accumulator as a 2-D fp32 tensor [rows][64] for the drain's tiled reduce-adds:
   // {32 columns x 32 rows} boxes in the 128-byte swizzle.
   CUtensorMap tdq;
@@ -675,13 +730,15 @@ bool sm100_bwd_supports(int dtype, int D) {
 size_t sm100_bwd_workspace_bytes(const Problem& p) { return sm100::bwd_layout(p).total; }
 
 int launch_bwd_sm100(int dtype, const Problem& p, TensorRef q, TensorRef k, TensorRef v,
-                     TensorRef dout, const float* lse, const float* delta, TensorRef dq,
+                     TensorRef out, TensorRef dout, const float* lse, float* delta, TensorRef dq,
                      TensorRef dk, TensorRef dv, float* dn, float* db, void* ws, size_t ws_bytes,
                      cudaStream_t st) {
   if (p.D != 64) return SSA_ERR_UNSUPPORTED;
   return dtype == SSA_DTYPE_BF16
-             ? sm100::run_bwd<true>(p, q, k, v, dout, lse, delta, dq, dk, dv, dn, db, ws, ws_bytes, st)
-             : sm100::run_bwd<false>(p, q, k, v, dout, lse, delta, dq, dk, dv, dn, db, ws, ws_bytes, st);
+             ? sm100::run_bwd<true>(p, q, k, v, out, dout, lse, delta, dq, dk, dv, dn, db, ws,
+                                    ws_bytes, st)
+             : sm100::run_bwd<false>(p, q, k, v, out, dout, lse, delta, dq, dk, dv, dn, db, ws,
+                                     ws_bytes, st);
 }
 
 }  // namespace ssa

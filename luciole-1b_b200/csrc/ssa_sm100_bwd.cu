@@ -561,14 +561,15 @@ __global__ void __launch_bounds__(512, 1)
 
 // Backward preprocess for the tensor-core path, one pass: delta = rowsum(O * dO) in fp32
 // (ssa_triton_kernel.py:267-298) and zeroing of the fp32 dQ accumulator rows (padding rows
-// included). 8 threads per row, 16-byte loads; 32 rows per 256-thread block.
-template <typename T>
+// included). D/8 threads per row, 16-byte loads; 2048/D rows per 256-thread block.
+template <typename T, int D>
 __global__ void __launch_bounds__(256) bwd_preprocess_sm100_kernel(Problem p, TensorRef o,
                                                                    TensorRef dout, float* delta,
                                                                    float* dq_accum,
                                                                    int64_t dq_rows) {
-  const int sub = threadIdx.x & 7;
-  const int rr = blockIdx.x * 32 + (threadIdx.x >> 3);  // row within the head's accumulator
+  constexpr int TPR = D / 8, RPB = 256 / TPR;
+  const int sub = threadIdx.x % TPR;
+  const int rr = blockIdx.x * RPB + threadIdx.x / TPR;  // row within the head's accumulator
   if (rr >= dq_rows) return;
   int z, hq, row, L;
   if (p.cu_seqlens) {  // accumulator rows are packed tokens; delta is [Hq][T]
@@ -583,7 +584,7 @@ __global__ void __launch_bounds__(256) bwd_preprocess_sm100_kernel(Problem p, Te
     L = p.N;
   }
   float4* zdst = reinterpret_cast<float4*>(
-      dq_accum + ((int64_t)blockIdx.y * dq_rows + rr) * 64 + sub * 8);
+      dq_accum + ((int64_t)blockIdx.y * dq_rows + rr) * D + sub * 8);
   zdst[0] = make_float4(0.f, 0.f, 0.f, 0.f);
   zdst[1] = make_float4(0.f, 0.f, 0.f, 0.f);
   float acc = 0.f;
@@ -599,9 +600,8 @@ __global__ void __launch_bounds__(256) bwd_preprocess_sm100_kernel(Problem p, Te
 #pragma unroll
     for (int i = 0; i < 8; ++i) acc = fmaf(to_f32<T>(ae[i]), to_f32<T>(be[i]), acc);
   }
-  acc += __shfl_xor_sync(0xffffffffu, acc, 1);
-  acc += __shfl_xor_sync(0xffffffffu, acc, 2);
-  acc += __shfl_xor_sync(0xffffffffu, acc, 4);
+#pragma unroll
+  for (int o2 = 1; o2 < TPR; o2 <<= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o2);
   if (valid && sub == 0) {
     const int64_t so = p.cu_seqlens ? (int64_t)hq * p.N + row : ((int64_t)z * p.Hq + hq) * p.N + row;
     delta[so] = acc;
@@ -609,18 +609,19 @@ __global__ void __launch_bounds__(256) bwd_preprocess_sm100_kernel(Problem p, Te
 }
 
 // dq (q's dtype, caller strides) = dq_accum (fp32) for the valid rows.
-template <typename T>
+template <typename T, int D>
 __global__ void __launch_bounds__(256) dq_convert_kernel(Problem p, const float* dq_accum,
                                                          int64_t dq_rows, TensorRef dq) {
+  constexpr int TPR = D / 8, RPB = 256 / TPR;
   const int z = blockIdx.y / p.Hq, hq = blockIdx.y % p.Hq;
   int seq_start, L;
   seq_bounds(p, z, seq_start, L);
-  const int row = blockIdx.x * 32 + (threadIdx.x >> 3);
-  const int d0 = (threadIdx.x & 7) * 8;
+  const int row = blockIdx.x * RPB + threadIdx.x / TPR;
+  const int d0 = (threadIdx.x % TPR) * 8;
   if (row >= L) return;
   const int64_t src_row = p.cu_seqlens ? (int64_t)hq * dq_rows + seq_start + row
                                        : ((int64_t)z * p.Hq + hq) * dq_rows + row;
-  const float4* s = reinterpret_cast<const float4*>(dq_accum + src_row * 64 + d0);
+  const float4* s = reinterpret_cast<const float4*>(dq_accum + src_row * D + d0);
   const float4 a0 = s[0], a1 = s[1];
   T* d = reinterpret_cast<T*>(dq.ptr) + row_offset(dq, p, z, hq, seq_start, row) + d0;
   uint4 w;
@@ -634,6 +635,474 @@ __global__ void __launch_bounds__(256) dq_convert_kernel(Problem p, const float*
   *reinterpret_cast<uint4*>(d) = w;
 }
 
+// ============================================================================================
+// Backward for D = 128. dK and dV alone take 256 TMEM columns here, so the D = 64 layout (two
+// S/dP buffers) does not fit. Instead:
+//   - query tiles are 64 rows; tile t belongs to P/dS warpgroup t & 1;
+//   - one S^T/dP^T buffer [0,128) is shared: the owning group pulls its 64 + 64 values per key
+//     row into registers and releases it (BB2_SL) before computing, so the next tile's S^T/dP^T
+//     MMAs overlap the current tile's arithmetic;
+//   - dQ^T = K^T dS^T (M = D = 128 lanes, N = 64 queries) per tile, drained per warp (32 head
+//     dims x 64 queries) with 2-D TMA reduce-adds into the fp32 accumulator.
+// TMEM: S^T [0,64), dP^T [64,128), dK [128,256), dV [256,384), dQ^T [384,448),
+//       P^T of group h (packed 16-bit) [448 + 32h, 480 + 32h).
+struct Bwd128Cfg {
+  static constexpr int D = 128;
+  static constexpr int BN = 128;  // key rows per CTA
+  static constexpr int BT = 64;   // query rows per tile
+  static constexpr int STAGES = 2;
+  static constexpr uint32_t KV_BYTES = BN * D * 2;   // 32 KB: two [128 x 128 B] slabs
+  static constexpr uint32_t KV_SLAB = BN * 128;      // 16 KB
+  static constexpr uint32_t QT_BYTES = BT * D * 2;   // 16 KB: two [64 x 128 B] slabs
+  static constexpr uint32_t QT_SLAB = BT * 128;      // 8 KB
+  static constexpr uint32_t DS_BYTES = BN * BT * 2;  // 16 KB: [128 keys x 64 queries]
+  static constexpr uint32_t DQS_WARP = BT * 32 * 4;  // 8 KB: [64 queries x 32 head dims] fp32
+  static constexpr uint32_t OFF_K = 0;
+  static constexpr uint32_t OFF_V = OFF_K + KV_BYTES;
+  static constexpr uint32_t OFF_Q = OFF_V + KV_BYTES;
+  static constexpr uint32_t OFF_DO = OFF_Q + STAGES * QT_BYTES;
+  static constexpr uint32_t OFF_DS = OFF_DO + STAGES * QT_BYTES;  // 2 buffers
+  static constexpr uint32_t OFF_DQS = OFF_DS + 2 * DS_BYTES;      // 4 warps x 8 KB
+  static constexpr uint32_t OFF_LSE = OFF_DQS + 4 * DQS_WARP;
+  static constexpr uint32_t OFF_DEL = OFF_LSE + STAGES * BT * 4;
+  static constexpr uint32_t OFF_BAR = OFF_DEL + STAGES * BT * 4;
+  static constexpr uint32_t SMEM_BYTES = OFF_BAR + 256 + 1024;
+  static constexpr uint32_t TMEM_COLS = 512;
+  static constexpr uint32_t COL_S = 0, COL_DP = 64, COL_DK = 128, COL_DV = 256, COL_DQ = 384,
+                            COL_PT = 448;
+  static constexpr int THREADS = 512;
+  static constexpr uint32_t REGS_PDS = 184, REGS_DQ = 88, REGS_CTRL = 56;  // 65536 in total
+  static constexpr int WARP_PRODUCER = 12, WARP_MMA = 13;
+};
+static_assert(Bwd128Cfg::SMEM_BYTES <= 232448, "shared memory budget");
+
+// Every barrier is waited on phase after phase by each of its waiters (a parity wait can only
+// tell two consecutive phases apart), hence one "S^T/dP^T ready" barrier per P/dS group.
+enum Bwd128Bar : int {
+  B2_KV = 0,
+  B2_QF = 1,    // 2 stages (stage t % 2 == group t & 1)
+  B2_QE = 3,    // 2 stages
+  B2_SF = 5,    // 2 groups: S^T/dP^T of the group's next tile in the shared buffer
+  B2_SL = 7,    // shared buffer read out by its owner (every tile, in order)
+  B2_SM = 8,    // 2 groups: P^T / dS^T written
+  B2_BF = 10,   // 2 groups: dV/dK MMAs of the group's last tile retired
+  B2_DSF = 12,  // 2 dS buffers: dQ^T MMA retired
+  B2_DQF = 14,
+  B2_DQE = 15,
+  B2_KVD = 16,
+  B2_END = 17,
+  B2_COUNT = 18
+};
+
+template <bool BF16>
+__global__ void __launch_bounds__(512, 1)
+    bwd128_sm100_kernel(const __grid_constant__ CUtensorMap tmQ,
+                        const __grid_constant__ CUtensorMap tmK,
+                        const __grid_constant__ CUtensorMap tmV,
+                        const __grid_constant__ CUtensorMap tmDO,
+                        const __grid_constant__ CUtensorMap tmDQ, const BwdArgs a) {
+  using C = Bwd128Cfg;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t bar0 = sbase + C::OFF_BAR;
+  auto bar = [&](int i) -> uint32_t { return bar0 + 8u * (uint32_t)i; };
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + C::OFF_BAR + 8 * B2_COUNT);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  float* lse_s = reinterpret_cast<float*>(smem + C::OFF_LSE);
+  float* del_s = reinterpret_cast<float*>(smem + C::OFF_DEL);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const Problem& p = a.p;
+  const int BHkv = p.B * p.Hkv;
+  const int kvb = (int)(blockIdx.x / BHkv);
+  const int bh = blockIdx.x % BHkv;
+  const int z = bh / p.Hkv, hkv = bh % p.Hkv;
+  int seq_start, L;
+  seq_bounds(p, z, seq_start, L);
+  const int n0 = kvb * C::BN;
+  if (n0 >= L || *reinterpret_cast<volatile unsigned int*>(a.status) != 0) {
+    if (threadIdx.x < 8 * p.gqa) {
+      const int g = threadIdx.x >> 3, sub = threadIdx.x & 7;
+      const int64_t pi = ((int64_t)z * p.Hq + hkv * p.gqa + g) * (8 * a.nkv) + 8 * kvb + sub;
+      a.dn_part[pi] = 0.f;
+      a.db_part[pi] = 0.f;
+    }
+    return;
+  }
+  const int q_start = p.causal ? n0 : 0;
+  const int T_h = (L - q_start + C::BT - 1) / C::BT;
+  const int T = T_h * p.gqa;
+  const int zc = p.cu_seqlens ? 0 : z;
+  // A P/dS group may own no tile of some q-head (tiles alternate between the groups): start
+  // every partial of this block at zero; the __syncthreads below orders these writes first.
+  if (threadIdx.x < 8 * p.gqa) {
+    const int g = threadIdx.x >> 3, sub = threadIdx.x & 7;
+    const int64_t pi = ((int64_t)z * p.Hq + hkv * p.gqa + g) * (8 * a.nkv) + 8 * kvb + sub;
+    a.dn_part[pi] = 0.f;
+    a.db_part[pi] = 0.f;
+  }
+
+  if (threadIdx.x == 0) {
+    mbar_init(bar(B2_KV), 1);
+    for (int s2 = 0; s2 < C::STAGES; ++s2) {
+      mbar_init(bar(B2_QF + s2), 33);
+      mbar_init(bar(B2_QE + s2), 1);
+    }
+    mbar_init(bar(B2_SL), 128);
+    for (int s2 = 0; s2 < 2; ++s2) {
+      mbar_init(bar(B2_SF + s2), 1);
+      mbar_init(bar(B2_SM + s2), 128);
+      mbar_init(bar(B2_BF + s2), 1);
+      mbar_init(bar(B2_DSF + s2), 1);
+    }
+    mbar_init(bar(B2_DQF), 1);
+    mbar_init(bar(B2_DQE), 128);
+    mbar_init(bar(B2_KVD), 1);
+    mbar_init(bar(B2_END), 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == C::WARP_PRODUCER) {
+    __syncwarp();
+    tmem_alloc(smem_u32(tmem_slot), C::TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp >= 12) {
+    regs_dec<C::REGS_CTRL>();
+    if (warp == C::WARP_PRODUCER) {
+      // ------------------------------------------------------------ producer (whole warp)
+      if (lane == 0) {
+        prefetch_tmap(&tmQ);
+        prefetch_tmap(&tmK);
+        prefetch_tmap(&tmV);
+        prefetch_tmap(&tmDO);
+        mbar_expect_tx(bar(B2_KV), 2 * C::KV_BYTES);
+#pragma unroll
+        for (int sl = 0; sl < 2; ++sl) {
+          tma_load_4d(sbase + C::OFF_K + sl * C::KV_SLAB, &tmK, bar(B2_KV), sl * 64,
+                      seq_start + n0, hkv, zc);
+          tma_load_4d(sbase + C::OFF_V + sl * C::KV_SLAB, &tmV, bar(B2_KV), sl * 64,
+                      seq_start + n0, hkv, zc);
+        }
+      }
+      int last_tile = -1;
+      float pl[2], pd[2];
+      auto fetch_stats = [&](int t) {
+        const int g = t / T_h, tt = t - g * T_h;
+        const int hq = hkv * p.gqa + g;
+        const int m0 = q_start + tt * C::BT;
+#pragma unroll
+        for (int k2 = 0; k2 < 2; ++k2) {
+          const int row = m0 + lane + 32 * k2;
+          pl[k2] = 0.f;
+          pd[k2] = 0.f;
+          if (row < L) {
+            const int64_t o = stat_offset(p, z, hq, seq_start, row);
+            pl[k2] = __ldg(a.lse + o);
+            pd[k2] = __ldg(a.delta + o);
+          }
+        }
+      };
+      fetch_stats(0);
+      for (int t = 0; t < T; ++t) {
+        const int st = t % C::STAGES, u = t / C::STAGES;
+        const int g = t / T_h, tt = t - g * T_h;
+        const int hq = hkv * p.gqa + g;
+        const int m0 = q_start + tt * C::BT;
+        bool ok = true;
+        if (t >= C::STAGES) ok = mbar_wait(bar(B2_QE + st), (u - 1) & 1, a.status);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok || *abort_flag) {
+          *abort_flag = 1;
+          break;
+        }
+        if (lane == 0) {
+          mbar_expect_tx(bar(B2_QF + st), 2 * C::QT_BYTES);
+#pragma unroll
+          for (int sl = 0; sl < 2; ++sl) {
+            tma_load_4d(sbase + C::OFF_Q + st * C::QT_BYTES + sl * C::QT_SLAB, &tmQ,
+                        bar(B2_QF + st), sl * 64, seq_start + m0, hq, zc);
+            tma_load_4d(sbase + C::OFF_DO + st * C::QT_BYTES + sl * C::QT_SLAB, &tmDO,
+                        bar(B2_QF + st), sl * 64, seq_start + m0, hq, zc);
+          }
+        }
+#pragma unroll
+        for (int k2 = 0; k2 < 2; ++k2) {
+          lse_s[st * C::BT + lane + 32 * k2] = pl[k2];
+          del_s[st * C::BT + lane + 32 * k2] = pd[k2];
+        }
+        mbar_arrive(bar(B2_QF + st));
+        last_tile = t;
+        if (t + 1 < T) fetch_stats(t + 1);
+      }
+      if (*abort_flag && lane == 0) {
+        mbar_wait(bar(B2_KV), 0, a.status);
+        for (int t = max(0, last_tile - C::STAGES + 1); t <= last_tile; ++t)
+          mbar_wait(bar(B2_QF + t % C::STAGES), (t / C::STAGES) & 1, a.status);
+      }
+    } else if (warp == C::WARP_MMA) {
+      // ------------------------------------------------------------ MMA issuer (converged)
+      const uint32_t leader = elect_one();
+      constexpr uint32_t id_s = idesc_f16(BF16, false, false, 128, 64);   // S^T, dP^T
+      constexpr uint32_t id_g = idesc_f16(BF16, false, true, 128, 128);   // dV, dK (N = D)
+      constexpr uint32_t id_q = idesc_f16(BF16, true, true, 128, 64);     // dQ^T
+      const uint32_t sK = sbase + C::OFF_K, sV = sbase + C::OFF_V;
+      auto wait_all = [&](uint32_t b, uint32_t par) {
+        return __all_sync(0xffffffffu, mbar_wait(b, par, a.status));
+      };
+      auto issue_sdp = [&](int t) {
+        const int st = t % C::STAGES;
+        const uint32_t qb = sbase + C::OFF_Q + st * C::QT_BYTES;
+        const uint32_t db = sbase + C::OFF_DO + st * C::QT_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t sl = kk >> 2, off = (kk & 3) * 32;
+          mma_ss_p(tmem + C::COL_S, sdesc_sw128(sK + sl * C::KV_SLAB + off, 16, 1024),
+                   sdesc_sw128(qb + sl * C::QT_SLAB + off, 16, 1024), id_s, kk > 0 ? 1u : 0u,
+                   leader);
+        }
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t sl = kk >> 2, off = (kk & 3) * 32;
+          mma_ss_p(tmem + C::COL_DP, sdesc_sw128(sV + sl * C::KV_SLAB + off, 16, 1024),
+                   sdesc_sw128(db + sl * C::QT_SLAB + off, 16, 1024), id_s, kk > 0 ? 1u : 0u,
+                   leader);
+        }
+        mma_commit_p(bar(B2_SF + (t & 1)), leader);
+      };
+      bool ok = wait_all(bar(B2_KV), 0) && wait_all(bar(B2_QF), 0);
+      if (ok) {
+        tc_fence_after();
+        issue_sdp(0);
+      }
+      for (int t = 0; ok && t < T; ++t) {
+        const int st = t % C::STAGES, h = t & 1;
+        // next tile's S^T/dP^T as soon as the owner has read the shared buffer
+        ok = wait_all(bar(B2_SL), t & 1);
+        if (ok && t + 1 < T) ok = wait_all(bar(B2_QF + (t + 1) % C::STAGES), ((t + 1) / C::STAGES) & 1);
+        if (!ok || *abort_flag) break;
+        tc_fence_after();
+        if (t + 1 < T) issue_sdp(t + 1);
+        ok = wait_all(bar(B2_SM + h), (t >> 1) & 1);
+        if (!ok || *abort_flag) break;
+        tc_fence_after();
+        const uint32_t qb = sbase + C::OFF_Q + st * C::QT_BYTES;
+        const uint32_t db = sbase + C::OFF_DO + st * C::QT_BYTES;
+        const uint32_t ds = sbase + C::OFF_DS + h * C::DS_BYTES;
+        // dV += P^T dO (A: TMEM, K = 64 queries); dK += dS^T Q (A: shared dS^T, K-major)
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          mma_ts_p(tmem + C::COL_DV, tmem + C::COL_PT + h * 32 + kk * 8,
+                   sdesc_sw128(db + kk * 2048, C::QT_SLAB, 1024), id_g, (t > 0 || kk > 0) ? 1u : 0u,
+                   leader);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)
+          mma_ss_p(tmem + C::COL_DK, sdesc_sw128(ds + kk * 32, 16, 1024),
+                   sdesc_sw128(qb + kk * 2048, C::QT_SLAB, 1024), id_g, (t > 0 || kk > 0) ? 1u : 0u,
+                   leader);
+        mma_commit_p(bar(B2_BF + h), leader);
+        // dQ^T = K^T dS^T (A: K read MN-major, M = head dims; B: dS^T, N = queries)
+        if (t >= 1) ok = wait_all(bar(B2_DQE), (t - 1) & 1);
+        if (!ok) break;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          mma_ss_p(tmem + C::COL_DQ, sdesc_sw128(sK + kk * 2048, C::KV_SLAB, 1024),
+                   sdesc_sw128(ds + kk * 2048, 8192, 1024), id_q, kk > 0 ? 1u : 0u, leader);
+        mma_commit_p(bar(B2_DQF), leader);
+        mma_commit_p(bar(B2_DSF + h), leader);
+        mma_commit_p(bar(B2_QE + st), leader);
+      }
+      if (!ok) *abort_flag = 1;
+      mma_commit_p(bar(B2_KVD), leader);
+      mma_commit_p(bar(B2_END), leader);
+      mbar_wait(bar(B2_END), 0, a.status);
+    }
+  } else if (warp < 8) {
+    // ------------------------------------------------------------ P / dS warp-groups
+    regs_inc<C::REGS_PDS>();
+    const int h = warp >> 2;
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;
+    const int j = n0 + r;
+    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    const uint32_t tS = tmem + lane_off + C::COL_S;
+    const uint32_t tP = tmem + lane_off + C::COL_DP;
+    const uint32_t tPT = tmem + lane_off + C::COL_PT + h * 32;
+    const float bval = __ldg(p.b_ptr);
+    const float cb = bval * p.scale;
+    float n = 0.f, nbs = 0.f;
+    float dn_acc[4] = {0.f, 0.f, 0.f, 0.f}, db_acc[4] = {0.f, 0.f, 0.f, 0.f};
+    bool ok = true;
+    const int qmin = p.causal ? j : 0;
+    for (int t = h; t < T; t += 2) {
+      const int st = t % C::STAGES;
+      const int g = t / T_h, tt = t - g * T_h;
+      const int hq = hkv * p.gqa + g;
+      n = load_n(p, hq);
+      nbs = n * bval * p.scale;
+      const int mh = q_start + tt * C::BT;
+      ok = mbar_wait(bar(B2_QF + st), (t / C::STAGES) & 1, a.status);
+      if (ok) ok = mbar_wait(bar(B2_SF + h), (t >> 1) & 1, a.status);
+      if (ok && t >= 2) ok = mbar_wait(bar(B2_DSF + h), ((t >> 1) - 1) & 1, a.status);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok || *abort_flag) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t s0[32], s1[32], d0[32], d1[32];
+      tmem_ld32(tS, s0);
+      tmem_ld32(tS + 32, s1);
+      tmem_ld32(tP, d0);
+      tmem_ld32(tP + 32, d1);
+      tmem_ld_wait_only();
+      tmem_pin_n(s0);
+      tmem_pin_n(s1);
+      tmem_pin_n(d0);
+      tmem_pin_n(d1);
+      tc_fence_before();
+      mbar_arrive(bar(B2_SL));  // the shared S^T/dP^T buffer may be overwritten now
+      const bool full = (!p.causal || mh >= n0 + C::BN - 1) && (mh + C::BT <= L) && (n0 + C::BN <= L);
+      const float* lrow = lse_s + st * C::BT;
+      const float* drow = del_s + st * C::BT;
+      uint8_t* dsrow = smem + C::OFF_DS + h * C::DS_BYTES + r * 128;
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        uint32_t pk[16], dk[16];
+        const uint32_t(&cs)[32] = c ? s1 : s0;
+        const uint32_t(&cd)[32] = c ? d1 : d0;
+        if (full)
+          bwd_chunk<32, BF16, false>(cs, cd, lrow + c * 32, drow + c * 32, n, cb, nbs, mh + c * 32,
+                                     qmin, L, j < L, dn_acc, db_acc, pk, dk);
+        else
+          bwd_chunk<32, BF16, true>(cs, cd, lrow + c * 32, drow + c * 32, n, cb, nbs, mh + c * 32,
+                                    qmin, L, j < L, dn_acc, db_acc, pk, dk);
+        if (c == 0) {  // dV of this group's previous tile must have read its P^T columns
+          bool okb = t < 2 || mbar_wait(bar(B2_BF + h), ((t >> 1) - 1) & 1, a.status);
+          if (!__all_sync(0xffffffffu, okb)) *abort_flag = 1;
+          tc_fence_after();
+        }
+        tmem_st16(tPT + c * 16, pk);
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+          const int chunk = c * 4 + q4;
+          *reinterpret_cast<uint4*>(dsrow + ((chunk ^ (r & 7)) << 4)) =
+              make_uint4(dk[q4 * 4], dk[q4 * 4 + 1], dk[q4 * 4 + 2], dk[q4 * 4 + 3]);
+        }
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      fence_proxy_async_smem();
+      mbar_arrive(bar(B2_SM + h));
+      // this group's last tile of q-head g: write its per-warp dn/db partials
+      const bool head_end = (tt + 2 >= T_h);
+      if (head_end) {
+        float x1 = (dn_acc[0] + dn_acc[1]) + (dn_acc[2] + dn_acc[3]);
+        float x2 = (db_acc[0] + db_acc[1]) + (db_acc[2] + db_acc[3]);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+          x1 += __shfl_xor_sync(0xffffffffu, x1, o);
+          x2 += __shfl_xor_sync(0xffffffffu, x2, o);
+        }
+        if (lane == 0) {
+          const int64_t pi = ((int64_t)z * p.Hq + hq) * (8 * a.nkv) + 8 * kvb + 4 * h + quad;
+          a.dn_part[pi] = x1 * kLn2;
+          a.db_part[pi] = x2 * n * p.scale;
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) dn_acc[i] = db_acc[i] = 0.f;
+      }
+    }
+    if (!ok) *abort_flag = 1;
+    // ---- epilogue: group 0 stores dK, group 1 stores dV (one key row per thread, 128 dims)
+    bool okd = ok && mbar_wait(bar(B2_KVD), 0, a.status);
+    okd = __all_sync(0xffffffffu, okd);
+    if (okd && !*abort_flag) {
+      tc_fence_after();
+      using Tout = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+      const TensorRef& dst = h ? a.dv : a.dk;
+      Tout* rowp = reinterpret_cast<Tout*>(dst.ptr) + row_offset(dst, p, z, hkv, seq_start, j);
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t o[32];
+        tmem_ld32(tmem + lane_off + (h ? C::COL_DV : C::COL_DK) + c * 32, o);
+        tmem_ld_wait(o);
+        if (j < L) {
+          uint32_t w[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            w[i] = pack2<BF16>(__uint_as_float(o[2 * i]), __uint_as_float(o[2 * i + 1]));
+          uint4* d4 = reinterpret_cast<uint4*>(rowp + c * 32);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) d4[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+        }
+      }
+    }
+  } else {
+    // ------------------------------------------------------------ dQ^T drain (warps 8..11)
+    // Warp `quad` owns head dims [32 quad, 32 quad + 32) (TMEM lanes): 64 queries x 32 dims of
+    // fp32 staged row-major (query-major) in its 8 KB, then one 2-D TMA reduce-add.
+    regs_dec<C::REGS_DQ>();
+    const int quad = warp & 3;
+    float* stage = reinterpret_cast<float*>(smem + C::OFF_DQS + quad * C::DQS_WARP);
+    const uint32_t stage_s = sbase + C::OFF_DQS + quad * C::DQS_WARP;
+    const uint32_t tQ = tmem + ((uint32_t)(quad * 32) << 16) + C::COL_DQ;
+    bool ok = true;
+    for (int t = 0; t < T; ++t) {
+      ok = mbar_wait(bar(B2_DQF), t & 1, a.status);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok || *abort_flag) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      uint32_t v0[32], v1[32];
+      tmem_ld32(tQ, v0);
+      tmem_ld32(tQ + 32, v1);
+      tmem_ld_wait_only();
+      tmem_pin(v0);
+      tmem_pin(v1);
+      tc_fence_before();
+      mbar_arrive(bar(B2_DQE));
+      if (lane == 0) bulk_wait_read0();
+      __syncwarp();
+#pragma unroll
+      for (int qi = 0; qi < 32; ++qi) stage[qi * 32 + lane] = __uint_as_float(v0[qi]);
+#pragma unroll
+      for (int qi = 0; qi < 32; ++qi) stage[(32 + qi) * 32 + lane] = __uint_as_float(v1[qi]);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        const int g = t / T_h, tt = t - g * T_h;
+        const int hq = hkv * p.gqa + g;
+        const int m0 = q_start + tt * C::BT;
+        const int row0 = p.cu_seqlens ? (int)((int64_t)hq * a.dq_rows + seq_start + m0)
+                                      : (int)(((int64_t)z * p.Hq + hq) * a.dq_rows + m0);
+        tma_reduce_add_2d(&tmDQ, stage_s, quad * 32, row0);
+        bulk_commit();
+      }
+    }
+    if (!ok) *abort_flag = 1;
+    if (lane == 0) bulk_wait0();
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == C::WARP_PRODUCER) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, C::TMEM_COLS);
+  }
+}
+
 struct BwdLayout {
   int nkv;
   int64_t dq_rows;
@@ -642,15 +1111,17 @@ struct BwdLayout {
 
 inline size_t al256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
+// Workspace of the tensor-core backward: the fp32 dQ accumulator (rows padded to 128 per head,
+// or 128 rows after the last packed token) and the dn/db partials.
 BwdLayout bwd_layout(const Problem& p) {
   BwdLayout l;
-  l.nkv = (p.max_seqlen + BwdCfg::BN - 1) / BwdCfg::BN;
+  l.nkv = (p.max_seqlen + 127) / 128;
   if (p.cu_seqlens) {
-    l.dq_rows = (int64_t)p.N + BwdCfg::BT;
-    l.dq_bytes = al256(sizeof(float) * (size_t)p.Hq * l.dq_rows * BwdCfg::D);
+    l.dq_rows = (int64_t)p.N + 128;
+    l.dq_bytes = al256(sizeof(float) * (size_t)p.Hq * l.dq_rows * p.D);
   } else {
-    l.dq_rows = (int64_t)((p.N + BwdCfg::BT - 1) / BwdCfg::BT) * BwdCfg::BT;
-    l.dq_bytes = al256(sizeof(float) * (size_t)p.B * p.Hq * l.dq_rows * BwdCfg::D);
+    l.dq_rows = (int64_t)((p.N + 127) / 128) * 128;
+    l.dq_bytes = al256(sizeof(float) * (size_t)p.B * p.Hq * l.dq_rows * p.D);
   }
   l.part_bytes = al256(sizeof(float) * (size_t)p.B * p.Hq * 8 * l.nkv);
   l.total = l.dq_bytes + 2 * l.part_bytes;
@@ -687,8 +1158,8 @@ int run_bwd(const Problem& p, TensorRef q, TensorRef k, TensorRef v, TensorRef o
   {
     using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
     dim3 gp((unsigned)((lay.dq_rows + 31) / 32), p.cu_seqlens ? p.Hq : p.B * p.Hq);
-    bwd_preprocess_sm100_kernel<T><<<gp, 256, 0, st>>>(p, out, dout, delta, a.dq_accum,
-                                                        lay.dq_rows);
+    bwd_preprocess_sm100_kernel<T, 64><<<gp, 256, 0, st>>>(p, out, dout, delta, a.dq_accum,
+                                                            lay.dq_rows);
     note_launches(1);
   }
   // dQ accumulator as a 2-D fp32 tensor [rows][64] for the drain's tiled reduce-adds:
@@ -715,8 +1186,67 @@ int run_bwd(const Problem& p, TensorRef q, TensorRef k, TensorRef v, TensorRef o
   kern<<<(unsigned)grid, C::THREADS, C::SMEM_BYTES, st>>>(tq, tk, tv, tdo, tdq, a);
   using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
   dim3 gc((p.max_seqlen + 31) / 32, p.B * p.Hq);
-  dq_convert_kernel<T><<<gc, 256, 0, st>>>(p, a.dq_accum, a.dq_rows, dq);
+  dq_convert_kernel<T, 64><<<gc, 256, 0, st>>>(p, a.dq_accum, a.dq_rows, dq);
   note_launches(2);
+  return launch_dndb_reduce(a.dn_part, a.db_part, p.B, p.Hq, 8 * lay.nkv, p.n_per_head, dn, db,
+                            st);
+}
+
+template <bool BF16>
+int run_bwd128(const Problem& p, TensorRef q, TensorRef k, TensorRef v, TensorRef out,
+               TensorRef dout, const float* lse, float* delta, TensorRef dq, TensorRef dk,
+               TensorRef dv, float* dn, float* db, void* ws, size_t ws_bytes, cudaStream_t st) {
+  using C = Bwd128Cfg;
+  using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+  const int dtype = BF16 ? SSA_DTYPE_BF16 : SSA_DTYPE_F16;
+  const BwdLayout lay = bwd_layout(p);
+  if (!ws || ws_bytes < lay.total) return SSA_ERR_WORKSPACE;
+  CUtensorMap tq, tk, tv, tdo, tdq;
+  int rc;
+  if ((rc = make_tmap_bhnd(&tq, q, p, dtype, p.Hq, C::BT)) != SSA_OK) return rc;
+  if ((rc = make_tmap_bhnd(&tk, k, p, dtype, p.Hkv, C::BN)) != SSA_OK) return rc;
+  if ((rc = make_tmap_bhnd(&tv, v, p, dtype, p.Hkv, C::BN)) != SSA_OK) return rc;
+  if ((rc = make_tmap_bhnd(&tdo, dout, p, dtype, p.Hq, C::BT)) != SSA_OK) return rc;
+  uint8_t* w = static_cast<uint8_t*>(ws);
+  BwdArgs a;
+  a.p = p;
+  a.dk = dk;
+  a.dv = dv;
+  a.lse = lse;
+  a.delta = delta;
+  a.dq_accum = reinterpret_cast<float*>(w);
+  a.dq_rows = lay.dq_rows;
+  a.dn_part = reinterpret_cast<float*>(w + lay.dq_bytes);
+  a.db_part = reinterpret_cast<float*>(w + lay.dq_bytes + lay.part_bytes);
+  a.status = device_status_ptr();
+  a.nkv = lay.nkv;
+  {
+    dim3 gp((unsigned)((lay.dq_rows + 15) / 16), p.cu_seqlens ? p.Hq : p.B * p.Hq);
+    bwd_preprocess_sm100_kernel<T, 128><<<gp, 256, 0, st>>>(p, out, dout, delta, a.dq_accum,
+                                                             lay.dq_rows);
+  }
+  {  // dQ accumulator as 2-D fp32 [rows][128]; {32 head dims x 64 queries} boxes, no swizzle
+    auto enc = tmap_encoder();
+    if (!enc) return SSA_ERR_CUDA;
+    const uint64_t rows = (uint64_t)(p.cu_seqlens ? p.Hq : p.B * p.Hq) * (uint64_t)lay.dq_rows;
+    cuuint64_t dims[2] = {(cuuint64_t)C::D, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)C::D * 4};
+    cuuint32_t box[2] = {32u, (cuuint32_t)C::BT};
+    cuuint32_t estr[2] = {1u, 1u};
+    if (enc(&tdq, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, a.dq_accum, dims, strides, box, estr,
+            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return SSA_ERR_CUDA;
+  }
+  auto kern = bwd128_sm100_kernel<BF16>;
+  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           (int)C::SMEM_BYTES) != cudaSuccess)
+    return SSA_ERR_CUDA;
+  const long long grid = (long long)lay.nkv * p.B * p.Hkv;
+  kern<<<(unsigned)grid, C::THREADS, C::SMEM_BYTES, st>>>(tq, tk, tv, tdo, tdq, a);
+  dim3 gc((p.max_seqlen + 15) / 16, p.B * p.Hq);
+  dq_convert_kernel<T, 128><<<gc, 256, 0, st>>>(p, a.dq_accum, a.dq_rows, dq);
+  note_launches(3);
   return launch_dndb_reduce(a.dn_part, a.db_part, p.B, p.Hq, 8 * lay.nkv, p.n_per_head, dn, db,
                             st);
 }
@@ -724,7 +1254,7 @@ int run_bwd(const Problem& p, TensorRef q, TensorRef k, TensorRef v, TensorRef o
 }  // namespace sm100
 
 bool sm100_bwd_supports(int dtype, int D) {
-  return (dtype == SSA_DTYPE_BF16 || dtype == SSA_DTYPE_F16) && D == 64;
+  return (dtype == SSA_DTYPE_BF16 || dtype == SSA_DTYPE_F16) && (D == 64 || D == 128);
 }
 
 size_t sm100_bwd_workspace_bytes(const Problem& p) { return sm100::bwd_layout(p).total; }
@@ -733,6 +1263,12 @@ int launch_bwd_sm100(int dtype, const Problem& p, TensorRef q, TensorRef k, Tens
                      TensorRef out, TensorRef dout, const float* lse, float* delta, TensorRef dq,
                      TensorRef dk, TensorRef dv, float* dn, float* db, void* ws, size_t ws_bytes,
                      cudaStream_t st) {
+  if (p.D == 128)
+    return dtype == SSA_DTYPE_BF16
+               ? sm100::run_bwd128<true>(p, q, k, v, out, dout, lse, delta, dq, dk, dv, dn, db,
+                                         ws, ws_bytes, st)
+               : sm100::run_bwd128<false>(p, q, k, v, out, dout, lse, delta, dq, dk, dv, dn, db,
+                                          ws, ws_bytes, st);
   if (p.D != 64) return SSA_ERR_UNSUPPORTED;
   return dtype == SSA_DTYPE_BF16
              ? sm100::run_bwd<true>(p, q, k, v, out, dout, lse, delta, dq, dk, dv, dn, db, ws,

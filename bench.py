@@ -45,12 +45,50 @@ for _p in (str(REPO), str(REPO / "luciole-1b_b200")):
 
 import torch  # noqa: E402
 
+# Workloads. c2 is the headline and the default; c3 / c4 are measured with
+# --config for the record. c3: packed documents, lengths seeded uniform in [128, 4096] until
+# 65,536 tokens (last one clipped); c4: one 32,768-token sequence at D = 128.
+CONFIGS = {
+    "c2": dict(B=8, HQ=32, HKV=8, S=2048, D=64, varlen=False,
+               workload="config2: SSA causal GQA fwd+bwd, B=8 Hq=32 Hkv=8 S=2048 D=64 bf16, per-head n",
+               metric="SSA attn fwd+bwd TFLOP/s (bf16, B=8 Hq=32 Hkv=8 S=2048 D=64 causal)"),
+    "c3": dict(B=1, HQ=32, HKV=8, S=65536, D=64, varlen=True,
+               workload="config3: SSA causal GQA fwd+bwd, packed documents 65536 tokens, lengths U[128,4096], Hq=32 Hkv=8 D=64 bf16",
+               metric="SSA attn fwd+bwd TFLOP/s (bf16, varlen 65536 tokens, Hq=32 Hkv=8 D=64 causal)"),
+    "c4": dict(B=1, HQ=32, HKV=8, S=32768, D=128, varlen=False,
+               workload="config4: SSA causal GQA fwd+bwd, B=1 Hq=32 Hkv=8 S=32768 D=128 bf16, per-head n",
+               metric="SSA attn fwd+bwd TFLOP/s (bf16, B=1 Hq=32 Hkv=8 S=32768 D=128 causal)"),
+}
+CFG = CONFIGS["c2"]
 B, HQ, HKV, S, D = 8, 32, 8, 2048, 64
 CAUSAL = True
 SSA_B = 0.8
-WORKLOAD = "config2: SSA causal GQA fwd+bwd, B=8 Hq=32 Hkv=8 S=2048 D=64 bf16, per-head n"
-METRIC = "SSA attn fwd+bwd TFLOP/s (bf16, B=8 Hq=32 Hkv=8 S=2048 D=64 causal)"
+WORKLOAD = CFG["workload"]
+METRIC = CFG["metric"]
 UNIT = "TFLOP/s"
+DOC_LENS = None  # varlen document lengths (c3)
+
+
+def select_config(name: str) -> None:
+    global CFG, B, HQ, HKV, S, D, WORKLOAD, METRIC, DOC_LENS
+    CFG = CONFIGS[name]
+    B, HQ, HKV, S, D = CFG["B"], CFG["HQ"], CFG["HKV"], CFG["S"], CFG["D"]
+    WORKLOAD, METRIC = CFG["workload"], CFG["metric"]
+    if CFG["varlen"]:
+        g = torch.Generator().manual_seed(3)
+        lens, tot = [], 0
+        while tot < S:
+            L = int(torch.randint(128, 4097, (1,), generator=g))
+            L = min(L, S - tot)
+            lens.append(L)
+            tot += L
+        DOC_LENS = lens
+
+
+def score_elements() -> float:
+    if DOC_LENS is not None:
+        return float(HQ * sum(L * L // 2 for L in DOC_LENS))
+    return float(B * HQ * (S * S // 2 if CAUSAL else S * S))
 
 # ncu DRAM traffic (read+write bytes) per launch of the dominant kernel (bwd_sm100_kernel),
 # taken from one ncu capture of this workload; None when no capture matches the current kernel.
@@ -58,13 +96,11 @@ NCU_TRAFFIC_BYTES = 1.518e9  # bwd_sm100_kernel, one ncu capture at config 2: dr
 
 
 def flops_per_rank() -> float:
-    E = B * HQ * (S * S // 2 if CAUSAL else S * S)
-    return 14.0 * D * E
+    return 14.0 * D * score_elements()
 
 
 def flops_bwd_per_rank() -> float:
-    E = B * HQ * (S * S // 2 if CAUSAL else S * S)
-    return 10.0 * D * E
+    return 10.0 * D * score_elements()
 
 
 def measured_peaks():
@@ -128,11 +164,18 @@ class ClockSampler:
 
 
 def make_inputs(device, seed):
+    """Seeded synthetic tensors: [B, H, S, D], or packed [T, H, D] for varlen."""
     g = torch.Generator(device="cpu").manual_seed(seed)
-    q = (torch.randn(B, HQ, S, D, generator=g) * 0.5).to(torch.bfloat16)
-    k = (torch.randn(B, HKV, S, D, generator=g) * 0.5).to(torch.bfloat16)
-    v = (torch.randn(B, HKV, S, D, generator=g) * 0.5).to(torch.bfloat16)
-    do = torch.randn(B, HQ, S, D, generator=g).to(torch.bfloat16)
+    if DOC_LENS is not None:
+        q = (torch.randn(S, HQ, D, generator=g) * 0.5).to(torch.bfloat16)
+        k = (torch.randn(S, HKV, D, generator=g) * 0.5).to(torch.bfloat16)
+        v = (torch.randn(S, HKV, D, generator=g) * 0.5).to(torch.bfloat16)
+        do = torch.randn(S, HQ, D, generator=g).to(torch.bfloat16)
+    else:
+        q = (torch.randn(B, HQ, S, D, generator=g) * 0.5).to(torch.bfloat16)
+        k = (torch.randn(B, HKV, S, D, generator=g) * 0.5).to(torch.bfloat16)
+        v = (torch.randn(B, HKV, S, D, generator=g) * 0.5).to(torch.bfloat16)
+        do = torch.randn(B, HQ, S, D, generator=g).to(torch.bfloat16)
     n = 0.3 + 0.3 * torch.rand(HQ, generator=g)
     return q, k, v, do, n
 
@@ -143,12 +186,13 @@ def cpu_oracle_sample(threads: int):
     from oracle.ssa_oracle import ssa_reference_grads
     torch.set_num_threads(threads)
     g = torch.Generator().manual_seed(123)
-    q = torch.randn(1, 1, S, D, generator=g) * 0.5
-    k = torch.randn(1, 1, S, D, generator=g) * 0.5
-    v = torch.randn(1, 1, S, D, generator=g) * 0.5
-    do = torch.randn(1, 1, S, D, generator=g)
+    Sc = min(S, 2048)  # a bounded sample: one q-head of one sequence of at most 2048 tokens
+    q = torch.randn(1, 1, Sc, D, generator=g) * 0.5
+    k = torch.randn(1, 1, Sc, D, generator=g) * 0.5
+    v = torch.randn(1, 1, Sc, D, generator=g) * 0.5
+    do = torch.randn(1, 1, Sc, D, generator=g)
     n, b = torch.tensor(0.43), torch.tensor(SSA_B)
-    flops = 14.0 * D * (S * S // 2)
+    flops = 14.0 * D * (Sc * Sc // 2)
     ssa_reference_grads(q, k, v, D ** -0.5, n, b, do, CAUSAL, compute_dtype=torch.float32)  # warm
     reps, t0 = 0, time.perf_counter()
     while True:
@@ -185,8 +229,8 @@ def run_reference(args):
         if i >= args.warmup:
             vals.append(v)
     val = statistics.median(vals)
-    sample = (f"one q-head of one sequence (S={S}, D={D}, causal) per step, fp32 eager "
-              f"restatement of the reference's SSA path with autograd")
+    sample = (f"one q-head of one sequence (S={min(S, 2048)}, D={D}, causal) per step, fp32 "
+              f"eager restatement of the reference's SSA path with autograd")
     line = {"impl": "reference", "metric": METRIC, "value": val, "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
@@ -201,15 +245,16 @@ def _one_ref_step(threads):
     from oracle.ssa_oracle import ssa_reference_grads
     torch.set_num_threads(threads)
     g = torch.Generator().manual_seed(7)
-    q = torch.randn(1, 1, S, D, generator=g) * 0.5
-    k = torch.randn(1, 1, S, D, generator=g) * 0.5
-    v = torch.randn(1, 1, S, D, generator=g) * 0.5
-    do = torch.randn(1, 1, S, D, generator=g)
+    Sc = min(S, 2048)
+    q = torch.randn(1, 1, Sc, D, generator=g) * 0.5
+    k = torch.randn(1, 1, Sc, D, generator=g) * 0.5
+    v = torch.randn(1, 1, Sc, D, generator=g) * 0.5
+    do = torch.randn(1, 1, Sc, D, generator=g)
     t0 = time.perf_counter()
     ssa_reference_grads(q, k, v, D ** -0.5, torch.tensor(0.43), torch.tensor(SSA_B), do, CAUSAL,
                         compute_dtype=torch.float32)
     el = time.perf_counter() - t0
-    fl = 14.0 * D * (S * S // 2)
+    fl = 14.0 * D * (Sc * Sc // 2)
     return fl / el / 1e12, el, fl, 1
 
 
@@ -220,8 +265,10 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    select_config(args.config)
     if args.impl == "reference":
         run_reference(args)
         return
@@ -234,16 +281,35 @@ def main():
     from SSA.ssa_triton_kernel import ssa_flash_attn_backward, ssa_flash_attn_forward
     import torch.distributed as dist
 
+    from SSA.ssa_triton_kernel import (ssa_flash_attn_varlen_backward,
+                                       ssa_flash_attn_varlen_forward)
     q_h, k_h, v_h, do_h, n_h = make_inputs(dev, seed=rank)
     q, k, v, do = (t.to(dev) for t in (q_h, k_h, v_h, do_h))
     n = n_h.to(dev)
     bb = torch.tensor(SSA_B, device=dev)
     scale = D ** -0.5
     red = torch.zeros(HQ + 1, device=dev)
+    if DOC_LENS is not None:
+        cu = torch.tensor([0] + list(torch.tensor(DOC_LENS).cumsum(0)), dtype=torch.int32,
+                          device=dev)
+        maxl = max(DOC_LENS)
+
+        def attn_fwd(q_, k_, v_):
+            return ssa_flash_attn_varlen_forward(q_, k_, v_, cu, maxl, scale, n, bb, CAUSAL)
+
+        def attn_bwd(q_, k_, v_, o_, do_, m_):
+            return ssa_flash_attn_varlen_backward(q_, k_, v_, o_, do_, m_, cu, maxl, scale, n, bb,
+                                                  CAUSAL)
+    else:
+        def attn_fwd(q_, k_, v_):
+            return ssa_flash_attn_forward(q_, k_, v_, scale, n, bb, causal=CAUSAL)
+
+        def attn_bwd(q_, k_, v_, o_, do_, m_):
+            return ssa_flash_attn_backward(q_, k_, v_, o_, do_, m_, scale, n, bb, causal=CAUSAL)
 
     def step():
-        out, m = ssa_flash_attn_forward(q, k, v, scale, n, bb, causal=CAUSAL)
-        dq, dk, dv, dn, db = ssa_flash_attn_backward(q, k, v, out, do, m, scale, n, bb, causal=CAUSAL)
+        out, m = attn_fwd(q, k, v)
+        dq, dk, dv, dn, db = attn_bwd(q, k, v, out, do, m)
         if world > 1:
             allreduce_ssa_param_grads(dn, db, buffer=red)
         return out, dq, dk, dv, dn, db
@@ -269,10 +335,9 @@ def main():
         for i in range(args.steps):
             e0, e1, e2 = ev[i]
             e0.record(st)
-            out, m = ssa_flash_attn_forward(q, k, v, scale, n, bb, causal=CAUSAL)
+            out, m = attn_fwd(q, k, v)
             e1.record(st)
-            dq, dk, dv, dn, db = ssa_flash_attn_backward(q, k, v, out, do, m, scale, n, bb,
-                                                         causal=CAUSAL)
+            dq, dk, dv, dn, db = attn_bwd(q, k, v, out, do, m)
             e2.record(st)
             if world > 1:
                 allreduce_ssa_param_grads(dn, db, buffer=red)
@@ -299,9 +364,8 @@ def main():
 
     def e2e_step():
         qd, kd, vd, dod = (t.to(dev, non_blocking=True) for t in (q_p, k_p, v_p, do_p))
-        out_, m_ = ssa_flash_attn_forward(qd, kd, vd, scale, n, bb, causal=CAUSAL)
-        dq_, dk_, dv_, dn_, db_ = ssa_flash_attn_backward(qd, kd, vd, out_, dod, m_, scale, n, bb,
-                                                          causal=CAUSAL)
+        out_, m_ = attn_fwd(qd, kd, vd)
+        dq_, dk_, dv_, dn_, db_ = attn_bwd(qd, kd, vd, out_, dod, m_)
         if world > 1:
             allreduce_ssa_param_grads(dn_, db_, buffer=red)
         red[:HQ].copy_(dn_)
@@ -332,8 +396,8 @@ def main():
         threads = os.cpu_count() or 1
         v_cpu, el, _, reps = cpu_oracle_sample(threads)
         cpu = {"value": v_cpu, "unit": UNIT, "cores": threads, "kind": "port",
-               "sample": f"{reps} x fwd+bwd of one q-head of one sequence (S={S}, D={D}, causal), "
-                         f"fp32 eager oracle with autograd, {el:.1f} s"}
+               "sample": f"{reps} x fwd+bwd of one q-head of one sequence (S={min(S, 2048)}, "
+                         f"D={D}, causal), fp32 eager oracle with autograd, {el:.1f} s"}
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
@@ -350,7 +414,7 @@ def main():
             "roofline": {"bound": "tensor", "kernel": "ssa_attn_bwd call (dominant)",
                          "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
                          "frac": achieved / peak_tf, "peak_kind": f"{peak_kind} bf16 burst",
-                         "traffic": NCU_TRAFFIC_BYTES},
+                         "traffic": NCU_TRAFFIC_BYTES if args.config == "c2" else None},
             "cpu_baseline": cpu,
             "clocks": clk.summary(),
             "gpu_launches": launches,

@@ -110,44 +110,47 @@ enum BwdBar : int {
 };
 
 // One W-query chunk of one key row: recompute P from S, dS = P (dP - delta) n b scale / (1+u),
-// accumulate dn/db (four independent partial sums each, to keep dependency chains short), and
-// pack P and dS to 16 bits. MASKED adds the causal / bounds test (valid iff the row is in range
-// and qmin <= q < L).
+// accumulate dn/db, and pack P and dS to 16 bits. The fp32 elementwise work runs on element
+// pairs with the packed f32x2 FMA/ADD/MUL instructions (half the issue slots); lrow / drow hold
+// -lse and -delta so both subtractions fold into packed FMA / ADD. MASKED adds the causal /
+// bounds test (valid iff the row is in range and qmin <= q < L).
 template <int W, bool BF16, bool MASKED>
 __device__ __forceinline__ void bwd_chunk(const uint32_t (&sx)[W], const uint32_t (&dp)[W],
                                           const float* lrow, const float* drow, float n, float cb,
                                           float nbs, int q0, int qmin, int L, bool row_ok,
-                                          float (&dn_acc)[4], float (&db_acc)[4],
+                                          float2 (&dn_acc)[2], float2 (&db_acc)[2],
                                           uint32_t (&pk)[W / 2], uint32_t (&dk)[W / 2]) {
+  const float2 n2 = make_float2(n, n), nbs2 = make_float2(nbs, nbs);
 #pragma unroll
   for (int e4 = 0; e4 < W / 4; ++e4) {
-    const float4 lv = *reinterpret_cast<const float4*>(lrow + e4 * 4);
-    const float4 dv = *reinterpret_cast<const float4*>(drow + e4 * 4);
-    const float lse4[4] = {lv.x, lv.y, lv.z, lv.w};
-    const float del4[4] = {dv.x, dv.y, dv.z, dv.w};
-    float pv[4], dsv[4];
+    const float4 nl = *reinterpret_cast<const float4*>(lrow + e4 * 4);
+    const float4 nd = *reinterpret_cast<const float4*>(drow + e4 * 4);
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      const int e = e4 * 4 + i;
-      const float x = __uint_as_float(sx[e]);
-      const float a1 = fmaf(fabsf(x), cb, 1.0f);
-      const float sl = copy_sign_bit(lg2_approx(a1), x);
-      float pr = ex2_approx(fmaf(n, sl, -lse4[i]));
+    for (int pi = 0; pi < 2; ++pi) {
+      const int e = e4 * 4 + pi * 2;
+      const float x0 = __uint_as_float(sx[e]), x1 = __uint_as_float(sx[e + 1]);
+      const float a0 = fmaf(fabsf(x0), cb, 1.0f), a1 = fmaf(fabsf(x1), cb, 1.0f);
+      const float2 sl = make_float2(copy_sign_bit(lg2_approx(a0), x0),
+                                    copy_sign_bit(lg2_approx(a1), x1));
+      const float2 nlse = pi ? make_float2(nl.z, nl.w) : make_float2(nl.x, nl.y);
+      const float2 ndel = pi ? make_float2(nd.z, nd.w) : make_float2(nd.x, nd.y);
+      const float2 t = __ffma2_rn(n2, sl, nlse);
+      float2 pr = make_float2(ex2_approx(t.x), ex2_approx(t.y));
       if (MASKED) {
         const int q = q0 + e;
-        pr = (row_ok && q >= qmin && q < L) ? pr : 0.f;
+        pr.x = (row_ok && q >= qmin && q < L) ? pr.x : 0.f;
+        pr.y = (row_ok && q + 1 >= qmin && q + 1 < L) ? pr.y : 0.f;
       }
-      const float dss = pr * (__uint_as_float(dp[e]) - del4[i]);
-      const float w = dss * rcp_approx(a1);
-      dn_acc[i] = fmaf(dss, sl, dn_acc[i]);
-      db_acc[i] = fmaf(w, x, db_acc[i]);
-      pv[i] = pr;
-      dsv[i] = w * nbs;
+      const float2 dss = __fmul2_rn(pr, __fadd2_rn(make_float2(__uint_as_float(dp[e]),
+                                                               __uint_as_float(dp[e + 1])),
+                                                   ndel));
+      const float2 w = __fmul2_rn(dss, make_float2(rcp_approx(a0), rcp_approx(a1)));
+      dn_acc[pi] = __ffma2_rn(dss, sl, dn_acc[pi]);
+      db_acc[pi] = __ffma2_rn(w, make_float2(x0, x1), db_acc[pi]);
+      const float2 dsv = __fmul2_rn(w, nbs2);
+      pk[e4 * 2 + pi] = pack2<BF16>(pr.x, pr.y);
+      dk[e4 * 2 + pi] = pack2<BF16>(dsv.x, dsv.y);
     }
-    pk[e4 * 2] = pack2<BF16>(pv[0], pv[1]);
-    pk[e4 * 2 + 1] = pack2<BF16>(pv[2], pv[3]);
-    dk[e4 * 2] = pack2<BF16>(dsv[0], dsv[1]);
-    dk[e4 * 2 + 1] = pack2<BF16>(dsv[2], dsv[3]);
   }
 }
 
@@ -277,8 +280,8 @@ __global__ void __launch_bounds__(512, 1)
       }
 #pragma unroll
       for (int k = 0; k < C::BT / 32; ++k) {
-        lse_s[st * C::BT + lane + 32 * k] = pl[k];
-        del_s[st * C::BT + lane + 32 * k] = pd[k];
+        lse_s[st * C::BT + lane + 32 * k] = -pl[k];  // stored negated for packed FMA / ADD
+        del_s[st * C::BT + lane + 32 * k] = -pd[k];
       }
       mbar_arrive(bar(BB_QF + st));
       last_tile = t;
@@ -386,7 +389,8 @@ __global__ void __launch_bounds__(512, 1)
     const float bval = __ldg(p.b_ptr);
     const float cb = bval * p.scale;
     float n = 0.f, nbs = 0.f;
-    float dn_acc[4] = {0.f, 0.f, 0.f, 0.f}, db_acc[4] = {0.f, 0.f, 0.f, 0.f};
+    float2 dn_acc[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+    float2 db_acc[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
     bool ok = true;
     for (int t = 0; t < T; ++t) {
       const int st = t % C::STAGES, dsb = t & 1;
@@ -456,8 +460,8 @@ __global__ void __launch_bounds__(512, 1)
       fence_proxy_async_smem();
       mbar_arrive(bar(BB_SM + h));
       if (tt == T_h - 1) {  // end of q-head g: each warp writes its dn/db partial
-        float x1 = (dn_acc[0] + dn_acc[1]) + (dn_acc[2] + dn_acc[3]);
-        float x2 = (db_acc[0] + db_acc[1]) + (db_acc[2] + db_acc[3]);
+        float x1 = (dn_acc[0].x + dn_acc[0].y) + (dn_acc[1].x + dn_acc[1].y);
+        float x2 = (db_acc[0].x + db_acc[0].y) + (db_acc[1].x + db_acc[1].y);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
           x1 += __shfl_xor_sync(0xffffffffu, x1, o);
@@ -469,7 +473,7 @@ __global__ void __launch_bounds__(512, 1)
           a.db_part[pi] = x2 * n * p.scale;
         }
 #pragma unroll
-        for (int i = 0; i < 4; ++i) dn_acc[i] = db_acc[i] = 0.f;
+        for (int i = 0; i < 2; ++i) dn_acc[i] = db_acc[i] = make_float2(0.f, 0.f);
       }
     }
     if (!ok) *abort_flag = 1;
@@ -835,8 +839,8 @@ __global__ void __launch_bounds__(512, 1)
         }
 #pragma unroll
         for (int k2 = 0; k2 < 2; ++k2) {
-          lse_s[st * C::BT + lane + 32 * k2] = pl[k2];
-          del_s[st * C::BT + lane + 32 * k2] = pd[k2];
+          lse_s[st * C::BT + lane + 32 * k2] = -pl[k2];  // stored negated (packed FMA / ADD)
+          del_s[st * C::BT + lane + 32 * k2] = -pd[k2];
         }
         mbar_arrive(bar(B2_QF + st));
         last_tile = t;
@@ -939,7 +943,8 @@ __global__ void __launch_bounds__(512, 1)
     const float bval = __ldg(p.b_ptr);
     const float cb = bval * p.scale;
     float n = 0.f, nbs = 0.f;
-    float dn_acc[4] = {0.f, 0.f, 0.f, 0.f}, db_acc[4] = {0.f, 0.f, 0.f, 0.f};
+    float2 dn_acc[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+    float2 db_acc[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
     bool ok = true;
     const int qmin = p.causal ? j : 0;
     for (int t = h; t < T; t += 2) {
@@ -1005,8 +1010,8 @@ __global__ void __launch_bounds__(512, 1)
       // this group's last tile of q-head g: write its per-warp dn/db partials
       const bool head_end = (tt + 2 >= T_h);
       if (head_end) {
-        float x1 = (dn_acc[0] + dn_acc[1]) + (dn_acc[2] + dn_acc[3]);
-        float x2 = (db_acc[0] + db_acc[1]) + (db_acc[2] + db_acc[3]);
+        float x1 = (dn_acc[0].x + dn_acc[0].y) + (dn_acc[1].x + dn_acc[1].y);
+        float x2 = (db_acc[0].x + db_acc[0].y) + (db_acc[1].x + db_acc[1].y);
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) {
           x1 += __shfl_xor_sync(0xffffffffu, x1, o);
@@ -1018,7 +1023,7 @@ __global__ void __launch_bounds__(512, 1)
           a.db_part[pi] = x2 * n * p.scale;
         }
 #pragma unroll
-        for (int i = 0; i < 4; ++i) dn_acc[i] = db_acc[i] = 0.f;
+        for (int i = 0; i < 2; ++i) dn_acc[i] = db_acc[i] = make_float2(0.f, 0.f);
       }
     }
     if (!ok) *abort_flag = 1;

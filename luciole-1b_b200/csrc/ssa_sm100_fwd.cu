@@ -264,41 +264,42 @@ __global__ void __launch_bounds__(192, 2)
         alpha = ex2_approx(m_run - ubound);
         m_run = ubound;
       }
-      const float neg_m = -m_run;
-      float rs0 = 0.f, rs1 = 0.f;
+      // P for element pairs: t2 - m on a packed f32x2 FMA, the row sum on packed adds.
+      const float2 n2 = make_float2(n, n), negm2 = make_float2(-m_run, -m_run);
+      float2 rs2 = make_float2(0.f, 0.f);
       uint32_t pk[C::BN / 64][32];
-      if (full) {
+      const int lim = p.causal ? min(L - 1, row) : L - 1;  // last visible key of this row
+      auto p_pair = [&](float x0, float x1) {
+        const float2 sl = make_float2(copy_sign_bit(lg2_approx(fmaf(fabsf(x0), cb, 1.0f)), x0),
+                                      copy_sign_bit(lg2_approx(fmaf(fabsf(x1), cb, 1.0f)), x1));
+        const float2 t = __ffma2_rn(n2, sl, negm2);
+        return make_float2(ex2_approx(t.x), ex2_approx(t.y));
+      };
+      if (full) {  // no masking code in interior blocks
 #pragma unroll
         for (int c = 0; c < C::BN / 32; ++c) {
 #pragma unroll
           for (int i = 0; i < 32; i += 2) {
-            const float x0 = __uint_as_float(sr[c][i]), x1 = __uint_as_float(sr[c][i + 1]);
-            const float p0 = ex2_approx(fmaf(n, copy_sign_bit(lg2_approx(fmaf(fabsf(x0), cb, 1.0f)), x0), neg_m));
-            const float p1 = ex2_approx(fmaf(n, copy_sign_bit(lg2_approx(fmaf(fabsf(x1), cb, 1.0f)), x1), neg_m));
-            rs0 += p0;
-            rs1 += p1;
-            pk[c >> 1][(c & 1) * 16 + (i >> 1)] = pack2<BF16>(p0, p1);
+            const float2 pp = p_pair(__uint_as_float(sr[c][i]), __uint_as_float(sr[c][i + 1]));
+            rs2 = __fadd2_rn(rs2, pp);
+            pk[c >> 1][(c & 1) * 16 + (i >> 1)] = pack2<BF16>(pp.x, pp.y);
           }
         }
       } else {
-        const int lim = p.causal ? min(L - 1, row) : L - 1;  // last visible key of this row
 #pragma unroll
         for (int c = 0; c < C::BN / 32; ++c) {
 #pragma unroll
           for (int i = 0; i < 32; i += 2) {
             const int col = n0 + c * 32 + i;
-            const float x0 = __uint_as_float(sr[c][i]), x1 = __uint_as_float(sr[c][i + 1]);
-            float p0 = ex2_approx(fmaf(n, copy_sign_bit(lg2_approx(fmaf(fabsf(x0), cb, 1.0f)), x0), neg_m));
-            float p1 = ex2_approx(fmaf(n, copy_sign_bit(lg2_approx(fmaf(fabsf(x1), cb, 1.0f)), x1), neg_m));
-            p0 = (col <= lim && row < L) ? p0 : 0.f;
-            p1 = (col + 1 <= lim && row < L) ? p1 : 0.f;
-            rs0 += p0;
-            rs1 += p1;
-            pk[c >> 1][(c & 1) * 16 + (i >> 1)] = pack2<BF16>(p0, p1);
+            float2 pp = p_pair(__uint_as_float(sr[c][i]), __uint_as_float(sr[c][i + 1]));
+            pp.x = (col <= lim && row < L) ? pp.x : 0.f;
+            pp.y = (col + 1 <= lim && row < L) ? pp.y : 0.f;
+            rs2 = __fadd2_rn(rs2, pp);
+            pk[c >> 1][(c & 1) * 16 + (i >> 1)] = pack2<BF16>(pp.x, pp.y);
           }
         }
       }
-      const float rs = rs0 + rs1;
+      const float rs = rs2.x + rs2.y;
       l_run = l_run * alpha + rs;
       // O correction. PV_{j-1} completed before S_j's commit fired (commit tracks every
       // earlier tcgen05 op of the issuing thread), so O is final for blocks < j here.

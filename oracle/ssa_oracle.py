@@ -37,6 +37,7 @@ kernels (``tests/golden/make_golden.py``).
 from __future__ import annotations
 
 
+import math
 from typing import Optional
 
 import torch
@@ -140,6 +141,47 @@ def ssa_reference_grads_varlen(q, k, v, cu_seqlens, softmax_scale: float, ssa_n,
         dn = dn + r["dn"]
         db = db + r["db"]
     return {"out": outs, "lse2": lse, "dq": dq, "dk": dk, "dv": dv, "dn": dn, "db": db}
+
+
+def ssa_pair_backward_with_lse(q, k, v, out, dout, lse2, softmax_scale: float, ssa_n, ssa_b,
+                               causal: bool, compute_dtype=torch.float64):
+    """Gradients of one (query block, key block) pair given the FINAL output and base-2
+    normaliser of the full rows -- the reference backward's per-block math
+    (ssa_triton_kernel.py:348-397 for dK/dV/dn/db, :444-477 for dQ):
+        P = exp2(t2 - M),  delta = rowsum(O dO),  ds_ssa = P (dO V^T - delta),
+        ds = ds_ssa n b / (1 + b|s|),  dV = P^T dO,  dK = ds^T Q scale,  dQ = ds K scale,
+        dn = sum ds_ssa sign(s) log1p(b|s|),  db = sum ds_ssa n sign(s) |s| / (1 + b|s|).
+    q/out/dout [B,Hq,Nq,D], k/v [B,Hkv,Nk,D], lse2 [B,Hq,Nq]. Returns (dq, dk, dv, dn, db)."""
+    cd = compute_dtype
+    bsz, hq, n_q, _ = q.shape
+    hkv = k.shape[1]
+    g = hq // hkv
+    qf, kf, vf = q.to(cd), k.repeat_interleave(g, dim=1).to(cd), v.repeat_interleave(g, dim=1).to(cd)
+    of, dof = out.to(cd), dout.to(cd)
+    s = torch.matmul(qf, kf.transpose(-1, -2)) * float(softmax_scale)
+    n_k = k.shape[2]
+    valid = torch.ones((n_q, n_k), dtype=torch.bool)
+    if causal:
+        valid = ~torch.triu(torch.ones((n_q, n_k), dtype=torch.bool), diagonal=1)
+    n_val = _expand_n(torch.as_tensor(ssa_n), hq, cd)
+    b_val = torch.as_tensor(ssa_b).to(cd)
+    sign, u = torch.sign(s), b_val * s.abs()
+    lg = torch.log1p(u)
+    t2 = n_val * sign * lg / math.log(2.0)
+    p = torch.where(valid, torch.exp2(t2 - lse2.to(cd).unsqueeze(-1)), torch.zeros_like(s))
+    delta = (of * dof).sum(-1, keepdim=True)
+    dp = torch.matmul(dof, vf.transpose(-1, -2))
+    ds_ssa = p * (dp - delta)
+    ds = ds_ssa * n_val * b_val / (1.0 + u)
+    dq = torch.matmul(ds, kf) * float(softmax_scale)
+    dk_full = torch.matmul(ds.transpose(-1, -2), qf) * float(softmax_scale)
+    dv_full = torch.matmul(p.transpose(-1, -2), dof)
+    dk = dk_full.reshape(bsz, hkv, g, n_k, -1).sum(2)
+    dv = dv_full.reshape(bsz, hkv, g, n_k, -1).sum(2)
+    dn_el = ds_ssa * sign * lg
+    dn = dn_el.sum() if torch.as_tensor(ssa_n).dim() == 0 else dn_el.sum(dim=(0, 2, 3))
+    db = (ds_ssa * n_val * s / (1.0 + u)).sum()
+    return dq, dk, dv, dn, db
 
 
 def causal_score_elements(B: int, Hq: int, N: int, causal: bool) -> int:

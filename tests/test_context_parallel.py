@@ -1,0 +1,156 @@
+"""Context-parallel ring SSA attention.
+
+CPU (gloo, world size 2): the ring schedule, zig-zag layout, base-2 merge of partial outputs and
+the travelling dK/dV accumulators, driven by the CPU oracle as the per-pair computation, must
+reproduce single-process full-sequence attention (out, dq, dk, dv, dn, db) to fp64 rounding.
+GPU (NCCL, 2 GPUs when available): the same ring on the CUDA kernels against the single-GPU
+kernels on the full sequence, within the bf16 tolerances of the parity tests.
+"""
+
+import os
+import socket
+import sys
+from pathlib import Path
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+REPO = Path(__file__).resolve().parent.parent
+
+
+def _port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def test_zigzag_split_and_gather_roundtrip():
+    from SSA.context_parallel import zigzag_gather, zigzag_split
+    x = torch.arange(2 * 3 * 48 * 4).reshape(2, 3, 48, 4)
+    for world in (1, 2, 3, 4):
+        parts = [zigzag_split(x, world, r) for r in range(world)]
+        assert torch.equal(zigzag_gather(parts), x)
+
+
+def _cpu_worker(rank, world, port, q, k, v, do, n, b, scale, out_q):
+    sys.path[:0] = [str(REPO), str(REPO / "luciole-1b_b200")]
+    import datetime
+    import torch.distributed as dist
+    from SSA.context_parallel import ring_ssa_backward, ring_ssa_forward, zigzag_split
+    from oracle.ssa_oracle import ssa_pair_backward_with_lse, ssa_reference_forward
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60))
+
+    def pair_fwd(q_, k_, v_, sc, n_, b_, causal):
+        return ssa_reference_forward(q_, k_, v_, sc, n_, b_, causal)
+
+    def pair_bwd(q_, k_, v_, o_, do_, l_, sc, n_, b_, causal):
+        return ssa_pair_backward_with_lse(q_, k_, v_, o_, do_, l_, sc, n_, b_, causal)
+
+    ql, kl, vl, dol = (zigzag_split(t, world, rank) for t in (q, k, v, do))
+    out, lse = ring_ssa_forward(ql, kl, vl, scale, n, b, pair_fwd=pair_fwd)
+    dq, dk, dv, dn, db = ring_ssa_backward(ql, kl, vl, out, dol, lse, scale, n, b,
+                                           pair_bwd=pair_bwd)
+    out_q.put((rank, out, dq, dk, dv, dn, db))
+    out_q.close()
+    out_q.join_thread()
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("per_head", [False, True])
+def test_ring_matches_full_sequence_cpu(per_head):
+    from SSA.context_parallel import zigzag_gather
+    from oracle.ssa_oracle import ssa_reference_grads
+    g = torch.Generator().manual_seed(21)
+    B, Hq, Hkv, S, D, world = 1, 4, 2, 64, 8, 2
+    q = torch.randn(B, Hq, S, D, generator=g, dtype=torch.float64)
+    k = torch.randn(B, Hkv, S, D, generator=g, dtype=torch.float64)
+    v = torch.randn(B, Hkv, S, D, generator=g, dtype=torch.float64)
+    do = torch.randn(B, Hq, S, D, generator=g, dtype=torch.float64)
+    n = torch.full((Hq,), 0.6, dtype=torch.float64) if per_head else torch.tensor(0.6, dtype=torch.float64)
+    b = torch.tensor(0.8, dtype=torch.float64)
+    full = ssa_reference_grads(q, k, v, 0.3, n, b, do, True)
+    ctx = mp.get_context("spawn")
+    out_q = ctx.Queue()
+    port = _port()
+    ps = [ctx.Process(target=_cpu_worker, args=(r, world, port, q, k, v, do, n, b, 0.3, out_q))
+          for r in range(world)]
+    for p in ps:
+        p.start()
+    res = sorted((out_q.get(timeout=180) for _ in ps), key=lambda t: t[0])
+    for p in ps:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for idx, name in ((1, "out"), (2, "dq"), (3, "dk"), (4, "dv")):
+        got = zigzag_gather([r[idx] for r in res])
+        assert torch.allclose(got, full[name], rtol=1e-9, atol=1e-10), name
+    for r in res:
+        assert torch.allclose(r[5], full["dn"], rtol=1e-9, atol=1e-10)
+        assert torch.allclose(r[6], full["db"], rtol=1e-9, atol=1e-10)
+
+
+def _gpu_worker(rank, world, port, q, k, v, do, n, b, scale, out_q):
+    sys.path[:0] = [str(REPO), str(REPO / "luciole-1b_b200")]
+    import datetime
+    import torch.distributed as dist
+    from SSA.context_parallel import ring_ssa_backward, ring_ssa_forward, zigzag_split
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=60), device_id=dev)
+    ql, kl, vl, dol = (zigzag_split(t, world, rank).to(dev) for t in (q, k, v, do))
+    out, lse = ring_ssa_forward(ql, kl, vl, scale, n.to(dev), b.to(dev))
+    dq, dk, dv, dn, db = ring_ssa_backward(ql, kl, vl, out, dol, lse, scale, n.to(dev), b.to(dev))
+    torch.cuda.synchronize()
+    out_q.put((rank, out.cpu(), dq.cpu(), dk.cpu(), dv.cpu(), dn.cpu(), db.cpu()))
+    out_q.close()
+    out_q.join_thread()
+    dist.barrier(device_ids=[rank])
+    dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+def test_ring_on_two_gpus_matches_single_gpu():
+    if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    from SSA.context_parallel import zigzag_gather
+    from SSA.ssa_triton_kernel import ssa_flash_attn_backward, ssa_flash_attn_forward
+    g = torch.Generator().manual_seed(5)
+    B, Hq, Hkv, S, D, world = 1, 8, 2, 4096, 128, 2
+    q = (torch.randn(B, Hq, S, D, generator=g) * 0.5).bfloat16()
+    k = (torch.randn(B, Hkv, S, D, generator=g) * 0.5).bfloat16()
+    v = (torch.randn(B, Hkv, S, D, generator=g) * 0.5).bfloat16()
+    do = torch.randn(B, Hq, S, D, generator=g).bfloat16()
+    n = 0.3 + 0.3 * torch.rand(Hq, generator=g)
+    b = torch.tensor(0.8)
+    scale = D ** -0.5
+    ctx = mp.get_context("spawn")
+    out_q = ctx.Queue()
+    port = _port()
+    ps = [ctx.Process(target=_gpu_worker, args=(r, world, port, q, k, v, do, n, b, scale, out_q))
+          for r in range(world)]
+    for p in ps:
+        p.start()
+    res = sorted((out_q.get(timeout=300) for _ in ps), key=lambda t: t[0])
+    for p in ps:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    dev = torch.device("cuda", 0)
+    o1, m1 = ssa_flash_attn_forward(q.to(dev), k.to(dev), v.to(dev), scale, n.to(dev), b.to(dev), True)
+    r1 = ssa_flash_attn_backward(q.to(dev), k.to(dev), v.to(dev), o1, do.to(dev), m1, scale,
+                                 n.to(dev), b.to(dev), True)
+    ref = dict(out=o1, dq=r1[0], dk=r1[1], dv=r1[2])
+    for idx, name in ((1, "out"), (2, "dq"), (3, "dk"), (4, "dv")):
+        got = zigzag_gather([r[idx] for r in res]).double()
+        want = ref[name].double().cpu()
+        d = (got - want).abs()
+        assert (d <= 2e-2 + 5e-2 * want.abs()).all(), (name, d.max().item())
+    for r in res:
+        assert torch.allclose(r[5].double(), r1[3].double().cpu(), rtol=2e-2, atol=2e-3)
+        assert torch.allclose(r[6].double(), r1[4].double().cpu(), rtol=2e-2, atol=2e-3)

@@ -270,6 +270,9 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
+    ap.add_argument("--cp", action="store_true",
+                    help="context-parallel ring over the ranks (strong scaling of one sequence; "
+                         "use with --config c4 under torchrun)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     select_config(args.config)
@@ -311,10 +314,30 @@ def main():
         def attn_bwd(q_, k_, v_, o_, do_, m_):
             return ssa_flash_attn_backward(q_, k_, v_, o_, do_, m_, scale, n, bb, causal=CAUSAL)
 
+    reduce_params = world > 1
+    if args.cp:
+        # Context parallel: every rank builds the same full sequence and keeps its zig-zag part;
+        # K/V travel around the ring, dn/db are reduced inside the ring backward.
+        from SSA.context_parallel import ring_ssa_backward, ring_ssa_forward, zigzag_split
+        if DOC_LENS is not None or world < 2:
+            raise SystemExit("--cp needs a dense config and at least 2 ranks")
+        full = make_inputs(dev, seed=0)
+        q_h, k_h, v_h, do_h = (zigzag_split(t, world, rank) for t in full[:4])
+        n_h = full[4]
+        q, k, v, do = (t.to(dev) for t in (q_h, k_h, v_h, do_h))
+        n = n_h.to(dev)
+        reduce_params = False
+
+        def attn_fwd(q_, k_, v_):
+            return ring_ssa_forward(q_, k_, v_, scale, n, bb)
+
+        def attn_bwd(q_, k_, v_, o_, do_, m_):
+            return ring_ssa_backward(q_, k_, v_, o_, do_, m_, scale, n, bb)
+
     def step():
         out, m = attn_fwd(q, k, v)
         dq, dk, dv, dn, db = attn_bwd(q, k, v, out, do, m)
-        if world > 1:
+        if reduce_params:
             allreduce_ssa_param_grads(dn, db, buffer=red)
         return out, dq, dk, dv, dn, db
 
@@ -343,7 +366,7 @@ def main():
             e1.record(st)
             dq, dk, dv, dn, db = attn_bwd(q, k, v, out, do, m)
             e2.record(st)
-            if world > 1:
+            if reduce_params:
                 allreduce_ssa_param_grads(dn, db, buffer=red)
         stop.record(st)
         barrier()
@@ -355,7 +378,8 @@ def main():
         t = torch.tensor([ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
-    value = flops_per_rank() * world / (ms * 1e-3) / 1e12
+    job_flops = flops_per_rank() * (1 if args.cp else world)  # cp: one sequence split
+    value = job_flops / (ms * 1e-3) / 1e12
 
     # ---- e2e: through the public API with pinned host buffers, copies inside the timed region.
     # Every step copies its inputs host->device and its results device->host; the copies run on
@@ -388,7 +412,7 @@ def main():
         qd, kd, vd, dod = dev_in[slot]
         out_, m_ = attn_fwd(qd, kd, vd)
         dq_, dk_, dv_, dn_, db_ = attn_bwd(qd, kd, vd, out_, dod, m_)
-        if world > 1:
+        if reduce_params:
             allreduce_ssa_param_grads(dn_, db_, buffer=red)
         res = torch.cat([dn_.reshape(-1), db_.reshape(1)])
         ev = torch.cuda.Event()
@@ -418,11 +442,11 @@ def main():
         t = torch.tensor([e2e_ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e_ms = float(t.item())
-    e2e_val = flops_per_rank() * world / (e2e_ms * 1e-3) / 1e12
+    e2e_val = job_flops / (e2e_ms * 1e-3) / 1e12
 
     status = _lib.load().ssa_device_status(_lib.stream_ptr(dev))
     peak_tf, _, peak_kind = measured_peaks()
-    achieved = flops_bwd_per_rank() / (t_bwd * 1e-3) / 1e12
+    achieved = flops_bwd_per_rank() / (world if args.cp else 1) / (t_bwd * 1e-3) / 1e12
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
@@ -434,10 +458,14 @@ def main():
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "global_batch": B * world, "seq_len": S,
+            "scaling": "strong" if args.cp else "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic",
+            "config": {"workload": WORKLOAD, "global_batch": B * (1 if args.cp else world),
+                       "seq_len": S,
                        "heads_q": HQ, "heads_kv": HKV, "head_dim": D, "causal": CAUSAL,
-                       "parallelism": f"batch-shard x{world} (weak), dn/db all-reduce",
+                       "parallelism": (f"context-parallel ring x{world} (zig-zag, NCCL P2P)"
+                                       if args.cp else
+                                       f"batch-shard x{world} (weak), dn/db all-reduce"),
                        "l2": "inputs larger than L2 (~300 MB resident per rank)"},
             "fwd_ms": t_fwd, "bwd_ms": t_bwd,
             "frac_of_peak": value / world / peak_tf,

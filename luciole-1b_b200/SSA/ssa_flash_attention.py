@@ -50,7 +50,9 @@ class SSAFlashAttnFunc(Function):
     @staticmethod
     def backward(ctx, dout):
         q, k, v, out, m, ssa_n_f32, ssa_b_f32 = ctx.saved_tensors
-        dout = dout.contiguous()
+        # The reference makes dout contiguous (ssa_flash_attention.py:56); the kernels take its
+        # strides, so a Megatron-layout gradient ([B, H, S, D] view of [S, B, H*D]) is read in
+        # place and only layouts the kernels cannot address are copied (in the kernel wrapper).
         dq, dk, dv, dn, db = ssa_flash_attn_backward(
             q, k, v, out, dout, m, ctx.softmax_scale, ssa_n_f32, ssa_b_f32, ctx.causal)
         dn = dn.reshape(ctx.n_meta[0]).to(ctx.n_meta[1])

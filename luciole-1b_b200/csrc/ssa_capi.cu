@@ -158,6 +158,25 @@ PFN_cuTensorMapEncodeTiled_v12000 tmap_encoder() {
   return fn;
 }
 
+// Makes the device that owns `ptr` current on the calling thread (its primary context). A thread
+// that has not used CUDA yet (an autograd worker thread, a fresh thread of a C caller) has no
+// current context: driver calls such as tensor-map encoding would fail there, and runtime calls
+// would default to device 0 whatever device the caller's tensors live on.
+int bind_device(const void* ptr, const char* name) {
+  cudaPointerAttributes at{};
+  if (cudaPointerGetAttributes(&at, ptr) != cudaSuccess) {
+    cudaGetLastError();
+    return fail(SSA_ERR_CUDA, "%s: cannot query the owning device of %p", name, ptr);
+  }
+  if (at.type != cudaMemoryTypeDevice && at.type != cudaMemoryTypeManaged)
+    return fail(SSA_ERR_CUDA, "%s: %p is not device memory", name, ptr);
+  if (cudaSetDevice(at.device) != cudaSuccess) {
+    cudaGetLastError();
+    return fail(SSA_ERR_CUDA, "%s: cannot make device %d current", name, at.device);
+  }
+  return SSA_OK;
+}
+
 unsigned int* device_status_ptr() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
@@ -180,6 +199,7 @@ int abi_validate_problem(const ssa_problem_t* pr) {
   return check_problem(pr);
 }
 Problem abi_to_problem(const ssa_problem_t* pr) { return to_problem(pr); }
+int abi_bind_device(const void* ptr, const char* name) { return bind_device(ptr, name); }
 int abi_error(int code, const char* fmt, ...) {
   va_list ap;
   va_start(ap, fmt);
@@ -222,6 +242,7 @@ int ssa_attn_fwd(const ssa_problem_t* prob, ssa_tensor_t q, ssa_tensor_t k, ssa_
       (rc = check_tensor(out, "out")))
     return rc;
   if (!lse) return fail(SSA_ERR_NULL, "lse is NULL");
+  if ((rc = bind_device(q.ptr, "q")) != SSA_OK) return rc;
   const Problem p = to_problem(prob);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (use_sm100(prob)) {
@@ -248,6 +269,7 @@ int ssa_attn_bwd_preprocess(const ssa_problem_t* prob, ssa_tensor_t out, ssa_ten
   if ((rc = check_problem(prob)) != SSA_OK) return rc;
   if ((rc = check_tensor(out, "out")) || (rc = check_tensor(dout, "dout"))) return rc;
   if (!delta) return fail(SSA_ERR_NULL, "delta is NULL");
+  if ((rc = bind_device(out.ptr, "out")) != SSA_OK) return rc;
   const Problem p = to_problem(prob);
   return finish_launch(launch_bwd_preprocess(prob->dtype, p, to_ref(out), to_ref(dout), delta,
                                              static_cast<cudaStream_t>(stream)),
@@ -276,6 +298,7 @@ int ssa_attn_bwd(const ssa_problem_t* prob, ssa_tensor_t q, ssa_tensor_t k, ssa_
   if (!workspace || workspace_bytes < need.total)
     return fail(SSA_ERR_WORKSPACE, "workspace needs %zu bytes, got %zu", need.total,
                 workspace_bytes);
+  if ((rc = bind_device(q.ptr, "q")) != SSA_OK) return rc;
   const BwdWorkspace w = carve_bwd(prob, workspace);
   const Problem p = to_problem(prob);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -306,6 +329,11 @@ int ssa_attn_bwd(const ssa_problem_t* prob, ssa_tensor_t q, ssa_tensor_t k, ssa_
 }
 
 int ssa_device_status(void* stream) {
+  int dev = -1;
+  if (cudaStreamGetDevice(static_cast<cudaStream_t>(stream), &dev) == cudaSuccess)
+    cudaSetDevice(dev);
+  else
+    cudaGetLastError();
   unsigned int* ptr = device_status_ptr();
   if (!ptr) return fail(SSA_ERR_CUDA, "cannot resolve the device status word");
   unsigned int h = 0;

@@ -43,5 +43,7 @@ void note_launches(int n);
 int abi_validate_problem(const ssa_problem_t* pr);
 Problem abi_to_problem(const ssa_problem_t* pr);
 int abi_error(int code, const char* fmt, ...);
+// Makes the device owning `ptr` current on the calling thread (see ssa_capi.cu).
+int abi_bind_device(const void* ptr, const char* name);
 
 }  // namespace ssa

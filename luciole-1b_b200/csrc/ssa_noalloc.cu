@@ -84,6 +84,7 @@ extern "C" int ssa_attn_bwd_noalloc(const ssa_problem_t* pr, ssa_tensor_t q, ssa
                      "the library's fixed %zu-byte device array; use ssa_attn_bwd with a "
                      "caller workspace",
                      need, kNoAllocScratchBytes);
+  if ((rc = abi_bind_device(q.ptr, "q")) != SSA_OK) return rc;
   void* base = nullptr;
   if (scratch_address(&base) != SSA_OK)
     return abi_error(SSA_ERR_CUDA, "ssa_attn_bwd_noalloc: cudaGetSymbolAddress failed");

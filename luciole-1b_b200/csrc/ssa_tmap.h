@@ -11,6 +11,7 @@
 #include <cudaTypedefs.h>
 
 #include "ssa_common.cuh"
+#include "ssa_internal.h"
 
 namespace ssa {
 
@@ -32,7 +33,9 @@ inline int make_tmap_bhnd(CUtensorMap* map, const TensorRef& t, const Problem& p
                           int H, int box_rows) {
   auto enc = tmap_encoder();
   if (!enc) return SSA_ERR_CUDA;
-  if (!tma_compatible(t, p, H)) return SSA_ERR_BAD_STRIDE;
+  if (!tma_compatible(t, p, H))
+    return abi_error(SSA_ERR_BAD_STRIDE, "tensor at %p: base and B/H/N strides must be 16-byte "
+                     "aligned for TMA", t.ptr);
   const uint64_t es = 2;
   const uint64_t B = p.cu_seqlens ? 1 : (uint64_t)p.B;
   const uint64_t rows = (uint64_t)p.N;
@@ -49,7 +52,15 @@ inline int make_tmap_bhnd(CUtensorMap* map, const TensorRef& t, const Problem& p
   CUresult r = enc(map, dt, 4, t.ptr, dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                    CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  return r == CUDA_SUCCESS ? SSA_OK : SSA_ERR_BAD_STRIDE;
+  if (r != CUDA_SUCCESS)
+    return abi_error(SSA_ERR_BAD_STRIDE,
+                     "cuTensorMapEncodeTiled failed (CUresult %d) for ptr %p dims {%llu, %llu, "
+                     "%llu, %llu} byte strides {%llu, %llu, %llu} box rows %d",
+                     (int)r, t.ptr, (unsigned long long)dims[0], (unsigned long long)dims[1],
+                     (unsigned long long)dims[2], (unsigned long long)dims[3],
+                     (unsigned long long)sN, (unsigned long long)sH, (unsigned long long)sB,
+                     box_rows);
+  return SSA_OK;
 }
 
 }  // namespace ssa

@@ -160,6 +160,66 @@ def test_strided_megatron_layout(cuda_device):
     assert_scalar_close("dn", r["dn"], ref["dn"])
 
 
+def test_megatron_layout_read_and_written_in_place(cuda_device):
+    """Layout fusion at the module boundary: q/k/v are read from [S, B, H, D] views, O is
+    written in [S, B, H, D] order (the module's [S, B, H*D] context is a view of the kernel's
+    output), and a gradient arriving as [S, B, H*D] is read in place as a strided dout."""
+    from SSA.ssa_triton_attention import SSAAttentionConfig, SSATritonAttention
+    K = _api()
+    S, B, Hq, Hkv, D = 384, 2, 8, 2, 64
+    qs = seeded((S, B, Hq, D), 61, 0.5).to(cuda_device)
+    ks = seeded((S, B, Hkv, D), 62, 0.5).to(cuda_device)
+    vs = seeded((S, B, Hkv, D), 63, 0.5).to(cuda_device)
+    g = seeded((S, B, Hq * D), 64).to(cuda_device)
+    q, k, v = (t.permute(1, 2, 0, 3) for t in (qs, ks, vs))
+    do = g.view(S, B, Hq, D).permute(1, 2, 0, 3)  # strided, not copied
+    n, b = torch.tensor(0.9, device=cuda_device), torch.tensor(0.8, device=cuda_device)
+    r = run_fwd_bwd(q, k, v, do, D ** -0.5, n, b, True)
+    assert r["out"].permute(2, 0, 1, 3).is_contiguous()
+    assert r["dq"].stride() == q.stride() and r["dk"].stride() == k.stride()
+    ref = ssa_reference_grads(q.cpu(), k.cpu(), v.cpu(), D ** -0.5, n.cpu(), b.cpu(), do.cpu(), True)
+    for name in ("out", "dq", "dk", "dv"):
+        assert_lowp_close(name, r[name], ref[name])
+    assert_scalar_close("dn", r["dn"], ref["dn"])
+    assert_scalar_close("db", r["db"], ref["db"])
+    cfg = SSAAttentionConfig(num_attention_heads=Hq, kv_channels=D, num_query_groups=Hkv)
+    mod = SSATritonAttention(cfg, layer_number=1, ssa_n=0.9, ssa_b=0.8).to(cuda_device)
+    ctx = mod(qs, ks, vs, None)
+    assert ctx.is_contiguous() and ctx._base is not None  # a view, no permute-back copy
+    assert ctx.data_ptr() == ctx._base.data_ptr()
+
+
+def test_backward_on_a_thread_without_cuda_context(cuda_device):
+    """Autograd runs backward on its own device threads; a thread that has not used CUDA yet has
+    no current context. The library binds the device owning the tensors itself, so the call
+    works there (and launches on that device) without the caller touching CUDA first."""
+    import threading
+    K = _api()
+    q = seeded((1, 4, 256, 64), 71, 0.5).to(cuda_device)
+    k = seeded((1, 2, 256, 64), 72, 0.5).to(cuda_device)
+    v = seeded((1, 2, 256, 64), 73, 0.5).to(cuda_device)
+    do = seeded((1, 4, 256, 64), 74).to(cuda_device)
+    n, b = torch.tensor(0.7, device=cuda_device), torch.tensor(0.8, device=cuda_device)
+    r = run_fwd_bwd(q, k, v, do, 0.125, n, b, True)
+    res = {}
+
+    def work():
+        try:
+            res["r"] = K.ssa_flash_attn_backward(q, k, v, r["out"], do, r["m"], 0.125, n, b,
+                                                 causal=True)
+            torch.cuda.synchronize(cuda_device)
+        except Exception as e:  # reported below
+            res["e"] = e
+
+    th = threading.Thread(target=work)
+    th.start()
+    th.join()
+    assert "e" not in res, repr(res.get("e"))
+    for name, got in zip(("dq", "dk", "dv", "dn", "db"), res["r"]):
+        ref = r[name]
+        assert torch.allclose(got.float(), ref.float(), rtol=2 ** -7, atol=1e-6), name
+
+
 def test_fp32_generic_path(cuda_device):
     """fp32 within 1e-5 relative (BASELINE config 1 shape, reduced batch*heads)."""
     q = seeded((1, 4, 512, 64), 21, 1.0, torch.float32)

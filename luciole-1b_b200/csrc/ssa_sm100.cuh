@@ -303,6 +303,40 @@ __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t saddr, uint32_t lbo_byt
   d |= (uint64_t)2 << 61;
   return d;
 }
+// The same descriptor split in two words. Every operand here uses the 128-byte swizzle with
+// SBO = 1024 B, so the high word (SBO >> 4 in bits 32-45, version bit 46, layout type 2 in bits
+// 61-63) is one constant and a descriptor is identified by its low word: start address >> 4 in
+// bits 0-13, LBO >> 4 in bits 16-29. Shared addresses stay below 2^18, so adding an offset >> 4
+// to the low word never carries out of the address field.
+constexpr uint32_t kDescHiSW128 = ((1024u >> 4) & 0x3FFFu) | (1u << 14) | (2u << 29);
+__device__ __forceinline__ uint32_t sdesc_lo(uint32_t saddr, uint32_t lbo_bytes) {
+  return ((saddr >> 4) & 0x3FFFu) | (((lbo_bytes >> 4) & 0x3FFFu) << 16);
+}
+// tcgen05.mma (A and B from shared memory) with descriptors given by their low words. Issued by
+// the calling thread alone (callers branch on an elected lane).
+__device__ __forceinline__ void mma_ss_lo(uint32_t d_tmem, uint32_t a_lo, uint32_t b_lo,
+                                          uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b64 da, db;\n\t"
+      "mov.b64 da, {%1, %5};\n\t"
+      "mov.b64 db, {%2, %5};\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_lo), "r"(b_lo), "r"(idesc), "r"(accumulate), "r"(kDescHiSW128)
+      : "memory");
+}
+// The same with A read from TMEM.
+__device__ __forceinline__ void mma_ts_lo(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_lo,
+                                          uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t.reg .b64 db;\n\t"
+      "mov.b64 db, {%2, %5};\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], db, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "r"(b_lo), "r"(idesc), "r"(accumulate), "r"(kDescHiSW128)
+      : "memory");
+}
+
 // Instruction descriptor for kind::f16 with fp32 accumulation.
 __host__ __device__ constexpr uint32_t idesc_f16(bool bf16, bool a_mn_major, bool b_mn_major,
                                                  int M, int N) {

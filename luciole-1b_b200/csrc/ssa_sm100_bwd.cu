@@ -294,37 +294,42 @@ __global__ void __launch_bounds__(512, 1)
     }
    } else if (warp == C::WARP_MMA) {
     // ---------------------------------------------------------------- MMA issuer
-    // The whole warp runs the schedule (waits, descriptor arithmetic); one elected lane issues
-    // each tcgen05.mma / commit through a predicate.
+    // The whole warp runs the schedule and its waits; one elected lane issues each batch of
+    // tcgen05.mma / commit. The warp shares its SM sub-partition with three busy warps, so the
+    // issue path is kept short: descriptors are low words (constant high word) advanced by
+    // immediates, computed once per CTA or per tile.
     {
-      const uint32_t leader = elect_one();
+      const bool leader = elect_one() != 0;
       constexpr uint32_t id_s = idesc_f16(BF16, false, false, 128, 64);  // S^T, dP^T
       constexpr uint32_t id_g = idesc_f16(BF16, false, true, 128, 64);   // dV, dK
       constexpr uint32_t id_q = idesc_f16(BF16, true, true, 128, 64);    // dQ
       const uint32_t sK = sbase + C::OFF_K, sV = sbase + C::OFF_V;
+      const uint32_t dK_s = sdesc_lo(sK, 16), dV_s = sdesc_lo(sV, 16);  // K-major K, V
+      const uint32_t dK_q = sdesc_lo(sK, 8192);                         // MN-major K (dQ's B)
       auto wait_all = [&](uint32_t b, uint32_t par) {
         return __all_sync(0xffffffffu, mbar_wait(b, par, a.status));
       };
+      // 16-byte units: a K step of 16 elements is 32 B within a swizzled row (2 units); a K step
+      // of 16 rows of an MN-major operand is 2048 B (128 units).
       auto issue_sdp = [&](int t, int h) {
+        if (!leader) return;
         const int st = t % C::STAGES;
-        const uint32_t qb = sbase + C::OFF_Q + st * C::QT_BYTES + h * C::HALF_BYTES;
-        const uint32_t db = sbase + C::OFF_DO + st * C::QT_BYTES + h * C::HALF_BYTES;
-        const uint32_t cs = h ? C::COL_S1 : C::COL_S0, cdp = h ? C::COL_DP1 : C::COL_DP0;
+        const uint32_t q_lo = sdesc_lo(sbase + C::OFF_Q + st * C::QT_BYTES + h * C::HALF_BYTES, 16);
+        const uint32_t o_lo = sdesc_lo(sbase + C::OFF_DO + st * C::QT_BYTES + h * C::HALF_BYTES, 16);
+        const uint32_t cs = tmem + (h ? C::COL_S1 : C::COL_S0);
+        const uint32_t cdp = tmem + (h ? C::COL_DP1 : C::COL_DP0);
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          mma_ss_p(tmem + cs, sdesc_sw128(sK + kk * 32, 16, 1024),
-                   sdesc_sw128(qb + kk * 32, 16, 1024), id_s, kk > 0 ? 1u : 0u, leader);
+        for (int kk = 0; kk < 4; ++kk) mma_ss_lo(cs, dK_s + 2 * kk, q_lo + 2 * kk, id_s, kk > 0);
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          mma_ss_p(tmem + cdp, sdesc_sw128(sV + kk * 32, 16, 1024),
-                   sdesc_sw128(db + kk * 32, 16, 1024), id_s, kk > 0 ? 1u : 0u, leader);
-        mma_commit_p(bar(BB_SF + h), leader);
+        for (int kk = 0; kk < 4; ++kk) mma_ss_lo(cdp, dV_s + 2 * kk, o_lo + 2 * kk, id_s, kk > 0);
+        mma_commit(bar(BB_SF + h));
       };
       bool ok = wait_all(bar(BB_KV), 0) && wait_all(bar(BB_QF), 0);
       if (ok) {
         tc_fence_after();
         issue_sdp(0, 0);
         issue_sdp(0, 1);
+        __syncwarp();
       }
       for (int t = 0; ok && t < T; ++t) {
         const int st = t % C::STAGES, dsb = t & 1;
@@ -339,39 +344,46 @@ __global__ void __launch_bounds__(512, 1)
             if (!ok) break;
             issue_sdp(t + 1, h);
           }
-          const uint32_t qb = sbase + C::OFF_Q + st * C::QT_BYTES + h * C::HALF_BYTES;
-          const uint32_t db = sbase + C::OFF_DO + st * C::QT_BYTES + h * C::HALF_BYTES;
-          const uint32_t dsh = sbase + C::OFF_DS + dsb * C::DS_BYTES + h * C::DS_SLAB;
-          // dV += P^T dO_h (P^T from TMEM); dK += dS^T Q_h (dS^T from the shared slab the dQ
-          // MMA also reads: [128 keys x 64 queries], K-major here, MN-major for dQ).
+          if (leader) {
+            const uint32_t q_mn = sdesc_lo(sbase + C::OFF_Q + st * C::QT_BYTES + h * C::HALF_BYTES, 8192);
+            const uint32_t o_mn = sdesc_lo(sbase + C::OFF_DO + st * C::QT_BYTES + h * C::HALF_BYTES, 8192);
+            const uint32_t ds_k = sdesc_lo(sbase + C::OFF_DS + dsb * C::DS_BYTES + h * C::DS_SLAB, 16);
+            const uint32_t acc0 = (t > 0 || h > 0) ? 1u : 0u;
+            // dV += P^T dO_h (P^T from TMEM); dK += dS^T Q_h (dS^T from the shared slab the dQ
+            // MMA also reads: [128 keys x 64 queries], K-major here, MN-major for dQ).
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            mma_ts_p(tmem + C::COL_DV, tmem + C::COL_PT + h * 32 + kk * 8,
-                     sdesc_sw128(db + kk * 2048, 8192, 1024), id_g,
-                     (t > 0 || h > 0 || kk > 0) ? 1u : 0u, leader);
+            for (int kk = 0; kk < 4; ++kk)
+              mma_ts_lo(tmem + C::COL_DV, tmem + C::COL_PT + h * 32 + kk * 8, o_mn + 128 * kk,
+                        id_g, kk > 0 ? 1u : acc0);
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            mma_ss_p(tmem + C::COL_DK, sdesc_sw128(dsh + kk * 32, 16, 1024),
-                     sdesc_sw128(qb + kk * 2048, 8192, 1024), id_g,
-                     (t > 0 || h > 0 || kk > 0) ? 1u : 0u, leader);
-          mma_commit_p(bar(BB_BF + h), leader);
+            for (int kk = 0; kk < 4; ++kk)
+              mma_ss_lo(tmem + C::COL_DK, ds_k + 2 * kk, q_mn + 128 * kk, id_g,
+                        kk > 0 ? 1u : acc0);
+            mma_commit(bar(BB_BF + h));
+          }
+          __syncwarp();
         }
         if (!ok || *abort_flag) break;
         if (t >= 1) ok = wait_all(bar(BB_DQE), (t - 1) & 1);
         if (!ok) break;
         tc_fence_after();
-        const uint32_t ds = sbase + C::OFF_DS + dsb * C::DS_BYTES;
+        if (leader) {
+          const uint32_t ds_mn = sdesc_lo(sbase + C::OFF_DS + dsb * C::DS_BYTES, C::DS_SLAB);
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          mma_ss_p(tmem + C::COL_DQ, sdesc_sw128(ds + kk * 2048, C::DS_SLAB, 1024),
-                   sdesc_sw128(sK + kk * 2048, 8192, 1024), id_q, kk > 0 ? 1u : 0u, leader);
-        mma_commit_p(bar(BB_DQF), leader);
-        mma_commit_p(bar(BB_DSF + dsb), leader);
-        mma_commit_p(bar(BB_QE + st), leader);
+          for (int kk = 0; kk < 8; ++kk)
+            mma_ss_lo(tmem + C::COL_DQ, ds_mn + 128 * kk, dK_q + 128 * kk, id_q, kk > 0);
+          mma_commit(bar(BB_DQF));
+          mma_commit(bar(BB_DSF + dsb));
+          mma_commit(bar(BB_QE + st));
+        }
+        __syncwarp();
       }
       if (!ok) *abort_flag = 1;
-      mma_commit_p(bar(BB_KVD), leader);
-      mma_commit_p(bar(BB_END), leader);
+      if (leader) {
+        mma_commit(bar(BB_KVD));
+        mma_commit(bar(BB_END));
+      }
+      __syncwarp();
       mbar_wait(bar(BB_END), 0, a.status);
     }
    }

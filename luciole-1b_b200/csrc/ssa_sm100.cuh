@@ -361,6 +361,23 @@ __device__ __forceinline__ float rcp_approx(float x) {
   asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+// 1/x for a pair of normal positive floats on the FMA pipe (packed f32x2), leaving the
+// special-function unit to lg2 / ex2. Seed: reflect the bit pattern through a constant,
+// r0 = bits^-1(C - bits(x)), which halves the exponent's sign and mirrors the mantissa
+// linearly; C = 0x7EF311C2 minimises max |x r0 - 1| over a binade (5.05e-2, found by exhaustive
+// search over C). Two Newton-Raphson steps r <- r + r (1 - x r) square the error each time:
+// max relative error 6.6e-6 (always from below).
+__device__ __forceinline__ float2 rcp2_newton(float2 x) {
+  float2 r = make_float2(__uint_as_float(0x7EF311C2u - __float_as_uint(x.x)),
+                         __uint_as_float(0x7EF311C2u - __float_as_uint(x.y)));
+  const float2 one = make_float2(1.f, 1.f), nx = make_float2(-x.x, -x.y);
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const float2 e = __ffma2_rn(nx, r, one);
+    r = __ffma2_rn(r, e, r);
+  }
+  return r;
+}
 // |y| with the sign bit of x (y >= 0 here): one LOP3.
 __device__ __forceinline__ float copy_sign_bit(float y, float x) {
   return __uint_as_float(__float_as_uint(y) | (__float_as_uint(x) & 0x80000000u));

@@ -10,11 +10,11 @@
 //
 // One CTA owns a 128-row key block of one (sequence, kv-head) and walks every q-head of its GQA
 // group (ssa_triton_kernel.py:573) and every 128-row query tile that can see the block. Per query
-// tile, the two 64-row halves are handled by two warp-groups in ping-pong:
-//   warp 12     TMA producer: K, V once; Q and dO tiles through a 2-stage ring; the tile's
+// tile, the two 64-row halves are handled by two warp-groups side by side:
+//   warp 12     TMA producer: K, V once; Q and dO tiles through a 3-stage ring; the tile's
 //               lse / delta rows into shared memory with plain loads.
 //   warp 13     MMA issuer (tcgen05, fp32 accumulation in TMEM):
-//                 S^T  = K Q_h^T,  dP^T = V dO_h^T          (SS, M=128 keys, N=64 queries)
+//                 S^T  = K Q^T,    dP^T = V dO^T            (SS, M=128 keys, N=128 queries)
 //                 dV  += P^T dO_h                           (TS: P^T read from TMEM)
 //                 dK  += dS^T Q_h                           (SS: dS^T from shared memory)
 //                 dQ   = dS K                               (SS, M=128 queries, dS from smem)
@@ -23,10 +23,12 @@
 //   warps 8..11 dQ drain: TMEM -> shared staging -> TMA bulk reduce-adds (fp32) into the
 //               dQ accumulator in global memory; a small kernel converts it to dq's dtype.
 // The roles sit on whole warpgroups so setmaxnreg can move registers to the P/dS groups.
-// TMEM (512 columns): S/dP for half 0 [0,128), for half 1 [128,256), dK [256,320),
-// dV [320,384), dQ [384,448), P^T (packed 16-bit) of half h at [448 + 32h, 480 + 32h). With
-// P^T outside the S/dP buffers and dS^T in shared memory, the next tile's S^T/dP^T MMAs can be
-// issued right behind the grads MMAs without waiting for them to retire.
+// TMEM (512 columns): S^T of the tile [0,128) and dP^T [128,256) (half h reads columns
+// [64h, 64h + 64) of each), dK [256,320), dV [320,384), dQ [384,448), P^T (packed 16-bit) of
+// half h at [448 + 32h, 480 + 32h). Each half pulls its S^T / dP^T into registers half-way
+// through its arithmetic and signals it, so the next tile's S^T / dP^T MMAs run under the second
+// half of the arithmetic; with P^T outside the S/dP buffers and dS^T in shared memory they do
+// not wait for the grads MMAs either.
 //
 // dn / db: per-thread fp32 sums, reduced per warp at the end of each q-head and written as
 // partials [z][hq][key block][half][warp]; a deterministic fp64 kernel sums them.
@@ -66,7 +68,7 @@ struct BwdCfg {
   static constexpr uint32_t OFF_BAR = OFF_DEL + STAGES * BT * 4;
   static constexpr uint32_t SMEM_BYTES = OFF_BAR + 256 + 1024;
   static constexpr uint32_t TMEM_COLS = 512;
-  static constexpr uint32_t COL_S0 = 0, COL_DP0 = 64, COL_S1 = 128, COL_DP1 = 192;
+  static constexpr uint32_t COL_S = 0, COL_DP = 128;  // S^T / dP^T of the whole tile
   static constexpr uint32_t COL_DK = 256, COL_DV = 320, COL_DQ = 384;
   static constexpr uint32_t COL_PT = 448;  // P^T (packed 16-bit) for half h at COL_PT + 32 h
   static constexpr int THREADS = 512;
@@ -98,23 +100,24 @@ enum BwdBar : int {
   BB_KV = 0,
   BB_QF = 1,    // 3 stages: Q/dO tile + lse/delta landed
   BB_QE = 4,    // 3 stages: tile's MMAs retired
-  BB_SF = 7,    // 2 halves: S^T and dP^T in TMEM
+  BB_SF = 7,    // S^T and dP^T of the tile in TMEM
+  BB_SC = 8,    // both halves pulled S^T / dP^T into registers (TMEM columns free)
   BB_SM = 9,    // 2 halves: P^T / dS^T written (TMEM + smem)
   BB_BF = 11,   // 2 halves: dV/dK MMAs of the half retired
-  BB_DSF = 13,  // 2 dS buffers: dQ MMA retired
-  BB_DQF = 15,  // dQ in TMEM
-  BB_DQE = 16,  // dQ read out of TMEM
-  BB_KVD = 17,  // all MMAs retired: dK, dV final
-  BB_END = 18,
-  BB_COUNT = 19
+  BB_DQF = 13,  // dQ in TMEM
+  BB_DQE = 14,  // dQ read out of TMEM
+  BB_KVD = 15,  // all MMAs retired: dK, dV final
+  BB_END = 16,
+  BB_COUNT = 17
 };
 
 // One W-query chunk of one key row: recompute P from S, dS = P (dP - delta) n b scale / (1+u),
 // accumulate dn/db, and pack P and dS to 16 bits. The fp32 elementwise work runs on element
 // pairs with the packed f32x2 FMA/ADD/MUL instructions (half the issue slots); lrow / drow hold
 // -lse and -delta so both subtractions fold into packed FMA / ADD. MASKED adds the causal /
-// bounds test (valid iff the row is in range and qmin <= q < L).
-template <int W, bool BF16, bool MASKED>
+// bounds test (valid iff the row is in range and qmin <= q < L). NRCP takes 1/(1+u) from
+// Newton steps on the FMA pipe instead of the special-function unit.
+template <int W, bool BF16, bool MASKED, bool NRCP>
 __device__ __forceinline__ void bwd_chunk(const uint32_t (&sx)[W], const uint32_t (&dp)[W],
                                           const float* lrow, const float* drow, float n, float cb,
                                           float nbs, int q0, int qmin, int L, bool row_ok,
@@ -144,7 +147,8 @@ __device__ __forceinline__ void bwd_chunk(const uint32_t (&sx)[W], const uint32_
       const float2 dss = __fmul2_rn(pr, __fadd2_rn(make_float2(__uint_as_float(dp[e]),
                                                                __uint_as_float(dp[e + 1])),
                                                    ndel));
-      const float2 w = __fmul2_rn(dss, make_float2(rcp_approx(a0), rcp_approx(a1)));
+      const float2 w = __fmul2_rn(
+          dss, NRCP ? rcp2_newton(make_float2(a0, a1)) : make_float2(rcp_approx(a0), rcp_approx(a1)));
       dn_acc[pi] = __ffma2_rn(dss, sl, dn_acc[pi]);
       db_acc[pi] = __ffma2_rn(w, make_float2(x0, x1), db_acc[pi]);
       const float2 dsv = __fmul2_rn(w, nbs2);
@@ -202,11 +206,11 @@ __global__ void __launch_bounds__(512, 1)
       mbar_init(bar(BB_QF + s), 33);
       mbar_init(bar(BB_QE + s), 1);
     }
+    mbar_init(bar(BB_SF), 1);
+    mbar_init(bar(BB_SC), 256);
     for (int s = 0; s < 2; ++s) {
-      mbar_init(bar(BB_SF + s), 1);
       mbar_init(bar(BB_SM + s), 128);
       mbar_init(bar(BB_BF + s), 1);
-      mbar_init(bar(BB_DSF + s), 1);
     }
     mbar_init(bar(BB_DQF), 1);
     mbar_init(bar(BB_DQE), 128);
@@ -300,7 +304,7 @@ __global__ void __launch_bounds__(512, 1)
     // immediates, computed once per CTA or per tile.
     {
       const bool leader = elect_one() != 0;
-      constexpr uint32_t id_s = idesc_f16(BF16, false, false, 128, 64);  // S^T, dP^T
+      constexpr uint32_t id_s = idesc_f16(BF16, false, false, 128, 128);  // S^T, dP^T
       constexpr uint32_t id_g = idesc_f16(BF16, false, true, 128, 64);   // dV, dK
       constexpr uint32_t id_q = idesc_f16(BF16, true, true, 128, 64);    // dQ
       const uint32_t sK = sbase + C::OFF_K, sV = sbase + C::OFF_V;
@@ -311,39 +315,44 @@ __global__ void __launch_bounds__(512, 1)
       };
       // 16-byte units: a K step of 16 elements is 32 B within a swizzled row (2 units); a K step
       // of 16 rows of an MN-major operand is 2048 B (128 units).
-      auto issue_sdp = [&](int t, int h) {
+      // S^T = K Q^T and dP^T = V dO^T for the whole 128-query tile: N = 128 runs at the full
+      // tensor rate, while an M = 128, K = 16 MMA costs about as long for any N up to 128.
+      auto issue_sdp = [&](int t) {
         if (!leader) return;
         const int st = t % C::STAGES;
-        const uint32_t q_lo = sdesc_lo(sbase + C::OFF_Q + st * C::QT_BYTES + h * C::HALF_BYTES, 16);
-        const uint32_t o_lo = sdesc_lo(sbase + C::OFF_DO + st * C::QT_BYTES + h * C::HALF_BYTES, 16);
-        const uint32_t cs = tmem + (h ? C::COL_S1 : C::COL_S0);
-        const uint32_t cdp = tmem + (h ? C::COL_DP1 : C::COL_DP0);
+        const uint32_t q_lo = sdesc_lo(sbase + C::OFF_Q + st * C::QT_BYTES, 16);
+        const uint32_t o_lo = sdesc_lo(sbase + C::OFF_DO + st * C::QT_BYTES, 16);
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) mma_ss_lo(cs, dK_s + 2 * kk, q_lo + 2 * kk, id_s, kk > 0);
+        for (int kk = 0; kk < 4; ++kk)
+          mma_ss_lo(tmem + C::COL_S, dK_s + 2 * kk, q_lo + 2 * kk, id_s, kk > 0);
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk) mma_ss_lo(cdp, dV_s + 2 * kk, o_lo + 2 * kk, id_s, kk > 0);
-        mma_commit(bar(BB_SF + h));
+        for (int kk = 0; kk < 4; ++kk)
+          mma_ss_lo(tmem + C::COL_DP, dV_s + 2 * kk, o_lo + 2 * kk, id_s, kk > 0);
+        mma_commit(bar(BB_SF));
       };
       bool ok = wait_all(bar(BB_KV), 0) && wait_all(bar(BB_QF), 0);
       if (ok) {
         tc_fence_after();
-        issue_sdp(0, 0);
-        issue_sdp(0, 1);
+        issue_sdp(0);
         __syncwarp();
       }
       for (int t = 0; ok && t < T; ++t) {
         const int st = t % C::STAGES, dsb = t & 1;
+        // The next tile's S^T / dP^T go first, as soon as both halves have pulled this tile's
+        // into registers (half-way through their arithmetic): the grads below read only P^T
+        // (own TMEM columns) and dS^T (shared memory).
+        if (t + 1 < T) {
+          ok = wait_all(bar(BB_QF + (t + 1) % C::STAGES), ((t + 1) / C::STAGES) & 1);
+          if (ok) ok = wait_all(bar(BB_SC), t & 1);
+          if (!ok || *abort_flag) break;
+          tc_fence_after();
+          issue_sdp(t + 1);
+          __syncwarp();
+        }
         for (int h = 0; h < 2 && ok; ++h) {
           ok = wait_all(bar(BB_SM + h), t & 1);
           if (!ok || *abort_flag) break;
           tc_fence_after();
-          // The next tile's S^T / dP^T go first: this half's buffer has been read by the P/dS
-          // group, and the grads below read only P^T (own TMEM columns) and dS^T (shared).
-          if (t + 1 < T) {
-            if (h == 0) ok = wait_all(bar(BB_QF + (t + 1) % C::STAGES), ((t + 1) / C::STAGES) & 1);
-            if (!ok) break;
-            issue_sdp(t + 1, h);
-          }
           if (leader) {
             const uint32_t q_mn = sdesc_lo(sbase + C::OFF_Q + st * C::QT_BYTES + h * C::HALF_BYTES, 8192);
             const uint32_t o_mn = sdesc_lo(sbase + C::OFF_DO + st * C::QT_BYTES + h * C::HALF_BYTES, 8192);
@@ -373,7 +382,6 @@ __global__ void __launch_bounds__(512, 1)
           for (int kk = 0; kk < 8; ++kk)
             mma_ss_lo(tmem + C::COL_DQ, ds_mn + 128 * kk, dK_q + 128 * kk, id_q, kk > 0);
           mma_commit(bar(BB_DQF));
-          mma_commit(bar(BB_DSF + dsb));
           mma_commit(bar(BB_QE + st));
         }
         __syncwarp();
@@ -395,56 +403,60 @@ __global__ void __launch_bounds__(512, 1)
     const int r = quad * 32 + lane;  // key row within the block
     const int j = n0 + r;
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
-    const uint32_t tS = tmem + lane_off + (h ? C::COL_S1 : C::COL_S0);
-    const uint32_t tP = tmem + lane_off + (h ? C::COL_DP1 : C::COL_DP0);
+    const uint32_t tS = tmem + lane_off + C::COL_S + 64 * h;
+    const uint32_t tP = tmem + lane_off + C::COL_DP + 64 * h;
     const uint32_t tPT = tmem + lane_off + C::COL_PT + h * 32;
     const float bval = __ldg(p.b_ptr);
     const float cb = bval * p.scale;
     float n = 0.f, nbs = 0.f;
     float2 dn_acc[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
     float2 db_acc[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
-    bool ok = true;
-    for (int t = 0; t < T; ++t) {
-      const int st = t % C::STAGES, dsb = t & 1;
-      const int g = t / T_h, tt = t - g * T_h;
+    // Tile t may start once its Q / dO / lse / delta have landed (QF) and its S^T / dP^T are in
+    // TMEM (SF). SF also implies that the dQ MMA of tile t - 2, which read this tile's dS^T
+    // buffer, has retired: its commit follows that MMA in the issuer's order.
+    auto wait_tile = [&](int t) {
+      bool w = mbar_wait(bar(BB_QF + t % C::STAGES), (t / C::STAGES) & 1, a.status);
+      if (w) w = mbar_wait(bar(BB_SF), t & 1, a.status);
+      w = __all_sync(0xffffffffu, w);
+      return w && !*abort_flag;
+    };
+    uint32_t sx[32], dp[32];
+    bool ok = wait_tile(0);
+    if (ok) {  // chunk 0 of tile 0; later tiles' chunk 0 is fetched behind the previous stores
+      tc_fence_after();
+      tmem_ld32(tS, sx);
+      tmem_ld32(tP, dp);
+    }
+    int st = 0, g = 0, tt = 0;  // ring stage, q-head within the group, tile within the head
+    for (int t = 0; ok && t < T; ++t) {
+      const int dsb = t & 1;
       const int hq = hkv * p.gqa + g;
       if (tt == 0) {
         n = load_n(p, hq);
         nbs = n * bval * p.scale;
       }
       const int mh = q_start + tt * C::BT + h * 64;  // first query row of this half
-      ok = mbar_wait(bar(BB_QF + st), (t / C::STAGES) & 1, a.status);
-      if (ok) ok = mbar_wait(bar(BB_SF + h), t & 1, a.status);
-      if (ok && t >= 2) ok = mbar_wait(bar(BB_DSF + dsb), ((t >> 1) - 1) & 1, a.status);
-      ok = __all_sync(0xffffffffu, ok);
-      if (!ok || *abort_flag) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
       const bool full = (!p.causal || mh >= n0 + C::BN - 1) && (mh + 64 <= L) && (n0 + C::BN <= L);
       const float* lrow = lse_s + st * C::BT + h * 64;
       const float* drow = del_s + st * C::BT + h * 64;
       uint8_t* dsrow = smem + C::OFF_DS + dsb * C::DS_BYTES + h * C::DS_SLAB + r * 128;
       const int qmin = p.causal ? j : 0;
-      // 2 chunks of 32 queries. Chunk 1's S / dP loads are issued after chunk 0 has been
-      // computed (so chunk 0 keeps every register for instruction-level parallelism) and are in
-      // flight while chunk 0's P^T and dS^T are stored.
-      uint32_t sx[32], dp[32];
-      tmem_ld32(tS, sx);
-      tmem_ld32(tP, dp);
       tmem_ld_wait_only();
       tmem_pin_n(sx);
       tmem_pin_n(dp);
+      // 2 chunks of 32 queries. Chunk 1's S / dP loads are issued after chunk 0 has been
+      // computed (so chunk 0 keeps every register for instruction-level parallelism) and are in
+      // flight while chunk 0's P^T and dS^T are stored; the next tile's chunk 0 is loaded while
+      // chunk 1's are stored.
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
         uint32_t pk[16], dk[16];
         if (full)
-          bwd_chunk<32, BF16, false>(sx, dp, lrow + c * 32, drow + c * 32, n, cb, nbs, mh + c * 32,
-                                     qmin, L, j < L, dn_acc, db_acc, pk, dk);
+          bwd_chunk<32, BF16, false, true>(sx, dp, lrow + c * 32, drow + c * 32, n, cb, nbs,
+                                           mh + c * 32, qmin, L, j < L, dn_acc, db_acc, pk, dk);
         else
-          bwd_chunk<32, BF16, true>(sx, dp, lrow + c * 32, drow + c * 32, n, cb, nbs, mh + c * 32,
-                                    qmin, L, j < L, dn_acc, db_acc, pk, dk);
+          bwd_chunk<32, BF16, true, true>(sx, dp, lrow + c * 32, drow + c * 32, n, cb, nbs,
+                                          mh + c * 32, qmin, L, j < L, dn_acc, db_acc, pk, dk);
         if (c == 0) {
           tmem_ld32(tS + 32, sx);
           tmem_ld32(tP + 32, dp);
@@ -465,6 +477,16 @@ __global__ void __launch_bounds__(512, 1)
           tmem_ld_wait_only();
           tmem_pin_n(sx);
           tmem_pin_n(dp);
+          tc_fence_before();
+          mbar_arrive(bar(BB_SC));  // this tile's S^T / dP^T columns may now be overwritten
+        } else if (t + 1 < T) {
+          if (wait_tile(t + 1)) {
+            tc_fence_after();
+            tmem_ld32(tS, sx);
+            tmem_ld32(tP, dp);
+          } else {
+            ok = false;
+          }
         }
       }
       tmem_st_wait();
@@ -486,6 +508,11 @@ __global__ void __launch_bounds__(512, 1)
         }
 #pragma unroll
         for (int i = 0; i < 2; ++i) dn_acc[i] = db_acc[i] = make_float2(0.f, 0.f);
+      }
+      st = st + 1 == C::STAGES ? 0 : st + 1;
+      if (++tt == T_h) {
+        tt = 0;
+        ++g;
       }
     }
     if (!ok) *abort_flag = 1;
@@ -997,10 +1024,10 @@ __global__ void __launch_bounds__(512, 1)
         const uint32_t(&cs)[32] = c ? s1 : s0;
         const uint32_t(&cd)[32] = c ? d1 : d0;
         if (full)
-          bwd_chunk<32, BF16, false>(cs, cd, lrow + c * 32, drow + c * 32, n, cb, nbs, mh + c * 32,
+          bwd_chunk<32, BF16, false, false>(cs, cd, lrow + c * 32, drow + c * 32, n, cb, nbs, mh + c * 32,
                                      qmin, L, j < L, dn_acc, db_acc, pk, dk);
         else
-          bwd_chunk<32, BF16, true>(cs, cd, lrow + c * 32, drow + c * 32, n, cb, nbs, mh + c * 32,
+          bwd_chunk<32, BF16, true, false>(cs, cd, lrow + c * 32, drow + c * 32, n, cb, nbs, mh + c * 32,
                                     qmin, L, j < L, dn_acc, db_acc, pk, dk);
         if (c == 0) {  // dV of this group's previous tile must have read its P^T columns
           bool okb = t < 2 || mbar_wait(bar(B2_BF + h), ((t >> 1) - 1) & 1, a.status);

@@ -102,13 +102,13 @@ enum BwdBar : int {
   BB_QE = 4,    // 3 stages: tile's MMAs retired
   BB_SF = 7,    // S^T and dP^T of the tile in TMEM
   BB_SC = 8,    // both halves pulled S^T / dP^T into registers (TMEM columns free)
-  BB_SM = 9,    // 2 halves: P^T / dS^T written (TMEM + smem)
-  BB_BF = 11,   // 2 halves: dV/dK MMAs of the half retired
-  BB_DQF = 13,  // dQ in TMEM
-  BB_DQE = 14,  // dQ read out of TMEM
-  BB_KVD = 15,  // all MMAs retired: dK, dV final
-  BB_END = 16,
-  BB_COUNT = 17
+  BB_SM = 9,    // P^T / dS^T of both halves written (TMEM + smem), and the previous
+                //   tile's dQ read out of TMEM by the drain warps (256 + 128 arrivals)
+  BB_BF = 10,   // dV / dK MMAs of the tile retired
+  BB_DQF = 11,  // dQ in TMEM
+  BB_KVD = 12,  // all MMAs retired: dK, dV final
+  BB_END = 13,
+  BB_COUNT = 14
 };
 
 // One W-query chunk of one key row: recompute P from S, dS = P (dP - delta) n b scale / (1+u),
@@ -208,12 +208,9 @@ __global__ void __launch_bounds__(512, 1)
     }
     mbar_init(bar(BB_SF), 1);
     mbar_init(bar(BB_SC), 256);
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(bar(BB_SM + s), 128);
-      mbar_init(bar(BB_BF + s), 1);
-    }
+    mbar_init(bar(BB_SM), 384);
+    mbar_init(bar(BB_BF), 1);
     mbar_init(bar(BB_DQF), 1);
-    mbar_init(bar(BB_DQE), 128);
     mbar_init(bar(BB_KVD), 1);
     mbar_init(bar(BB_END), 1);
     *abort_flag = 0;
@@ -349,35 +346,32 @@ __global__ void __launch_bounds__(512, 1)
           issue_sdp(t + 1);
           __syncwarp();
         }
-        for (int h = 0; h < 2 && ok; ++h) {
-          ok = wait_all(bar(BB_SM + h), t & 1);
-          if (!ok || *abort_flag) break;
-          tc_fence_after();
-          if (leader) {
-            const uint32_t q_mn = sdesc_lo(sbase + C::OFF_Q + st * C::QT_BYTES + h * C::HALF_BYTES, 8192);
-            const uint32_t o_mn = sdesc_lo(sbase + C::OFF_DO + st * C::QT_BYTES + h * C::HALF_BYTES, 8192);
-            const uint32_t ds_k = sdesc_lo(sbase + C::OFF_DS + dsb * C::DS_BYTES + h * C::DS_SLAB, 16);
-            const uint32_t acc0 = (t > 0 || h > 0) ? 1u : 0u;
-            // dV += P^T dO_h (P^T from TMEM); dK += dS^T Q_h (dS^T from the shared slab the dQ
-            // MMA also reads: [128 keys x 64 queries], K-major here, MN-major for dQ).
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-              mma_ts_lo(tmem + C::COL_DV, tmem + C::COL_PT + h * 32 + kk * 8, o_mn + 128 * kk,
-                        id_g, kk > 0 ? 1u : acc0);
-#pragma unroll
-            for (int kk = 0; kk < 4; ++kk)
-              mma_ss_lo(tmem + C::COL_DK, ds_k + 2 * kk, q_mn + 128 * kk, id_g,
-                        kk > 0 ? 1u : acc0);
-            mma_commit(bar(BB_BF + h));
-          }
-          __syncwarp();
-        }
+        // Both halves' P^T / dS^T written, and dQ(t-1) read out of TMEM by the drain warps
+        // (they arrive on the same barrier): the grads and this tile's dQ can go.
+        const uint32_t q_mn = sdesc_lo(sbase + C::OFF_Q + st * C::QT_BYTES, 8192);
+        const uint32_t o_mn = sdesc_lo(sbase + C::OFF_DO + st * C::QT_BYTES, 8192);
+        const uint32_t ds_k = sdesc_lo(sbase + C::OFF_DS + dsb * C::DS_BYTES, 16);
+        const uint32_t ds_mn = sdesc_lo(sbase + C::OFF_DS + dsb * C::DS_BYTES, C::DS_SLAB);
+        ok = wait_all(bar(BB_SM), t & 1);
         if (!ok || *abort_flag) break;
-        if (t >= 1) ok = wait_all(bar(BB_DQE), (t - 1) & 1);
-        if (!ok) break;
         tc_fence_after();
         if (leader) {
-          const uint32_t ds_mn = sdesc_lo(sbase + C::OFF_DS + dsb * C::DS_BYTES, C::DS_SLAB);
+          // dV += P^T dO_h (P^T from TMEM); dK += dS^T Q_h (dS^T from the shared slab the dQ
+          // MMA also reads: [128 keys x 64 queries] per half, K-major here, MN-major for dQ).
+          // Half 0 before half 1, always: dK / dV are bit-reproducible.
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            const uint32_t acc0 = (t > 0 || h > 0) ? 1u : 0u;
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+              mma_ts_lo(tmem + C::COL_DV, tmem + C::COL_PT + h * 32 + kk * 8,
+                        o_mn + (C::HALF_BYTES >> 4) * h + 128 * kk, id_g, kk > 0 ? 1u : acc0);
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+              mma_ss_lo(tmem + C::COL_DK, ds_k + (C::DS_SLAB >> 4) * h + 2 * kk,
+                        q_mn + (C::HALF_BYTES >> 4) * h + 128 * kk, id_g, kk > 0 ? 1u : acc0);
+          }
+          mma_commit(bar(BB_BF));
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk)
             mma_ss_lo(tmem + C::COL_DQ, ds_mn + 128 * kk, dK_q + 128 * kk, id_q, kk > 0);
@@ -461,7 +455,7 @@ __global__ void __launch_bounds__(512, 1)
           tmem_ld32(tS + 32, sx);
           tmem_ld32(tP + 32, dp);
           // dV(t-1) must have read this half's P^T columns before they are rewritten.
-          bool okb = t == 0 || mbar_wait(bar(BB_BF + h), (t - 1) & 1, a.status);
+          bool okb = t == 0 || mbar_wait(bar(BB_BF), (t - 1) & 1, a.status);
           if (!__all_sync(0xffffffffu, okb)) *abort_flag = 1;
           tc_fence_after();
         }
@@ -492,7 +486,7 @@ __global__ void __launch_bounds__(512, 1)
       tmem_st_wait();
       tc_fence_before();
       fence_proxy_async_smem();
-      mbar_arrive(bar(BB_SM + h));
+      mbar_arrive(bar(BB_SM));
       if (tt == T_h - 1) {  // end of q-head g: each warp writes its dn/db partial
         float x1 = (dn_acc[0].x + dn_acc[0].y) + (dn_acc[1].x + dn_acc[1].y);
         float x2 = (db_acc[0].x + db_acc[0].y) + (db_acc[1].x + db_acc[1].y);
@@ -549,6 +543,9 @@ __global__ void __launch_bounds__(512, 1)
     uint8_t* stage = smem + C::OFF_DQS + quad * C::DQS_WARP;
     const uint32_t stage_s = sbase + C::OFF_DQS + quad * C::DQS_WARP;
     const uint32_t tQ = tmem + ((uint32_t)(quad * 32) << 16) + C::COL_DQ;
+    // The drain's arrival for tile t's barrier SM(t) says dQ(t-1) has left TMEM; tile 0 has no
+    // predecessor.
+    mbar_arrive(bar(BB_SM));
     bool ok = true;
     for (int t = 0; t < T; ++t) {
       ok = mbar_wait(bar(BB_DQF), t & 1, a.status);
@@ -565,7 +562,7 @@ __global__ void __launch_bounds__(512, 1)
       tmem_pin(v0);
       tmem_pin(v1);
       tc_fence_before();
-      mbar_arrive(bar(BB_DQE));
+      mbar_arrive(bar(BB_SM));  // dQ(t) is out of TMEM: counts toward SM(t + 1)
       const int g = t / T_h, tt = t - g * T_h;
       const int hq = hkv * p.gqa + g;
       const int m0 = q_start + tt * C::BT + quad * 32;

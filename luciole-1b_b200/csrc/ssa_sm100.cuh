@@ -378,6 +378,28 @@ __device__ __forceinline__ float2 rcp2_newton(float2 x) {
   }
   return r;
 }
+// 2^t for a pair of t in [-125, 126] on the FMA pipe (packed f32x2), to take part of the exponentials off
+// the special-function unit. t = j + f with j = rint(t): adding and subtracting 1.5 * 2^23 rounds
+// in the FP adder and leaves j in the low bits of the sum; f in [-0.5, 0.5]. 2^f comes from a
+// degree-4 polynomial, a relative-error minimax fit on [-0.5, 0.5] (Lawson's iteratively
+// reweighted least squares; max relative error 2.7e-6 evaluated in fp32), and 2^j enters through
+// an integer add on the exponent field. t is clamped at -125 so the scaled result stays normal
+// (below that 2^t is returned as 2^-125, a negligible weight next to the row's maximum).
+__device__ __forceinline__ float2 exp2_poly2(float2 t) {
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+  t = make_float2(fmaxf(t.x, -125.0f), fmaxf(t.y, -125.0f));
+  const float2 z = __fadd2_rn(t, make_float2(kRound, kRound));
+  const float2 j = __fadd2_rn(z, make_float2(-kRound, -kRound));
+  const float2 f = __fadd2_rn(t, make_float2(-j.x, -j.y));
+  float2 q = __ffma2_rn(make_float2(0.009570101276f, 0.009570101276f), f,
+                        make_float2(0.05591786280f, 0.05591786280f));
+  q = __ffma2_rn(q, f, make_float2(0.2402474433f, 0.2402474433f));
+  q = __ffma2_rn(q, f, make_float2(0.6931217909f, 0.6931217909f));
+  q = __ffma2_rn(q, f, make_float2(0.9999992847f, 0.9999992847f));
+  // The low bits of z hold j (two's complement, |j| < 2^22); shifted into the exponent field.
+  return make_float2(__uint_as_float(__float_as_uint(q.x) + (__float_as_uint(z.x) << 23)),
+                     __uint_as_float(__float_as_uint(q.y) + (__float_as_uint(z.y) << 23)));
+}
 // |y| with the sign bit of x (y >= 0 here): one LOP3.
 __device__ __forceinline__ float copy_sign_bit(float y, float x) {
   return __uint_as_float(__float_as_uint(y) | (__float_as_uint(x) & 0x80000000u));

@@ -32,6 +32,8 @@ namespace ssa {
 namespace sm100 {
 
 constexpr float kRescaleThreshold = 8.0f;
+// Element pairs, of every 4, whose exponential is evaluated on the FMA pipe (exp2_poly2).
+constexpr int kEmuPairs = 2;
 
 template <int D>
 struct FwdCfg {
@@ -269,18 +271,21 @@ __global__ void __launch_bounds__(192, 2)
       float2 rs2 = make_float2(0.f, 0.f);
       uint32_t pk[C::BN / 64][32];
       const int lim = p.causal ? min(L - 1, row) : L - 1;  // last visible key of this row
-      auto p_pair = [&](float x0, float x1) {
+      // kEmuPairs of every 4 element pairs take 2^t from the FMA-pipe polynomial, the rest from
+      // the special-function unit, which lg2 keeps busy as well.
+      auto p_pair = [&](float x0, float x1, bool emu) {
         const float2 sl = make_float2(copy_sign_bit(lg2_approx(fmaf(fabsf(x0), cb, 1.0f)), x0),
                                       copy_sign_bit(lg2_approx(fmaf(fabsf(x1), cb, 1.0f)), x1));
         const float2 t = __ffma2_rn(n2, sl, negm2);
-        return make_float2(ex2_approx(t.x), ex2_approx(t.y));
+        return emu ? exp2_poly2(t) : make_float2(ex2_approx(t.x), ex2_approx(t.y));
       };
       if (full) {  // no masking code in interior blocks
 #pragma unroll
         for (int c = 0; c < C::BN / 32; ++c) {
 #pragma unroll
           for (int i = 0; i < 32; i += 2) {
-            const float2 pp = p_pair(__uint_as_float(sr[c][i]), __uint_as_float(sr[c][i + 1]));
+            const float2 pp = p_pair(__uint_as_float(sr[c][i]), __uint_as_float(sr[c][i + 1]),
+                                     ((i >> 1) & 3) < kEmuPairs);
             rs2 = __fadd2_rn(rs2, pp);
             pk[c >> 1][(c & 1) * 16 + (i >> 1)] = pack2<BF16>(pp.x, pp.y);
           }
@@ -291,7 +296,8 @@ __global__ void __launch_bounds__(192, 2)
 #pragma unroll
           for (int i = 0; i < 32; i += 2) {
             const int col = n0 + c * 32 + i;
-            float2 pp = p_pair(__uint_as_float(sr[c][i]), __uint_as_float(sr[c][i + 1]));
+            float2 pp = p_pair(__uint_as_float(sr[c][i]), __uint_as_float(sr[c][i + 1]),
+                               ((i >> 1) & 3) < kEmuPairs);
             pp.x = (col <= lim && row < L) ? pp.x : 0.f;
             pp.y = (col + 1 <= lim && row < L) ? pp.y : 0.f;
             rs2 = __fadd2_rn(rs2, pp);

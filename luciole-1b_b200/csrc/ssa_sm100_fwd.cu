@@ -8,9 +8,10 @@
 // One CTA = one 128-row query tile of one (sequence, q-head). 6 warps:
 //   warp 0      TMEM allocator + TMA producer (Q once, K/V through a 2-stage ring)
 //   warp 1      MMA issuer: S = Q K^T (SS form, fp32 in TMEM), O += P V (TS form: P read
-//               straight from TMEM, where it overwrote S)
+//               straight from TMEM). P has its own columns, so S_{j+1} is issued as soon as the
+//               softmax warps hold S_j in registers and runs under their work on block j.
 //   warps 2..5  one thread per query row: tcgen05.ld its S row, SSA transform, running max
-//               and sum, P (bf16/f16) written back into TMEM, O correction, epilogue.
+//               and sum, P (bf16/f16) written to TMEM, O correction, epilogue.
 // Two CTAs share an SM (TMEM 2 x 256 columns, ~81 KB shared memory each), so one CTA's
 // transcendental work overlaps the other's tensor-core work.
 //
@@ -33,7 +34,10 @@ namespace sm100 {
 
 constexpr float kRescaleThreshold = 8.0f;
 // Element pairs, of every 4, whose exponential is evaluated on the FMA pipe (exp2_poly2).
-constexpr int kEmuPairs = 2;
+// Measured on B200: D = 128 gains from 2 of 4; at D = 64 the softmax is not bound by the
+// special-function unit and the extra FMA-pipe work only costs time.
+template <int D>
+constexpr int kEmuPairs = D == 128 ? 2 : 0;
 
 template <int D>
 struct FwdCfg {
@@ -49,10 +53,11 @@ struct FwdCfg {
   static constexpr uint32_t OFF_BAR = OFF_V + STAGES * KV_BYTES;
   static constexpr uint32_t SMEM_BYTES = OFF_BAR + 256 + 1024;  // + slack for 1 KB alignment
   static constexpr uint32_t TMEM_COLS = 256;
-  static constexpr uint32_t COL_S = 0;   // S (fp32, BN columns); P (packed 16-bit) aliases it
-  static constexpr uint32_t COL_O = BN;  // O accumulator (fp32, D columns)
+  static constexpr uint32_t COL_S = 0;            // S (fp32, BN columns)
+  static constexpr uint32_t COL_P = BN;           // P (packed 16-bit, BN / 2 columns)
+  static constexpr uint32_t COL_O = BN + BN / 2;  // O accumulator (fp32, D columns)
   static constexpr int THREADS = 192;
-  static_assert(BN + D <= (int)TMEM_COLS, "TMEM budget");
+  static_assert(BN + BN / 2 + D <= (int)TMEM_COLS, "TMEM budget");
 };
 
 struct FwdArgs {
@@ -68,11 +73,12 @@ enum FwdBar : int {
   FB_KF = 1,   // 2 stages
   FB_VF = 3,   // 2 stages
   FB_KVE = 5,  // 2 stages
-  FB_S = 7,
-  FB_P = 8,
-  FB_O = 9,
-  FB_END = 10,
-  FB_COUNT = 11
+  FB_S = 7,    // S_j in TMEM
+  FB_SC = 8,   // S_j pulled into registers by the softmax warps: its columns are free
+  FB_P = 9,    // P_j in TMEM (and O corrected for block j)
+  FB_O = 10,   // P_j V_j retired: O final through block j, P columns free
+  FB_END = 11,
+  FB_COUNT = 12
 };
 
 template <int D, bool BF16>
@@ -114,6 +120,7 @@ __global__ void __launch_bounds__(192, 2)
       mbar_init(bar(FB_KVE + s), 1);
     }
     mbar_init(bar(FB_S), 1);
+    mbar_init(bar(FB_SC), 128);
     mbar_init(bar(FB_P), 128);
     mbar_init(bar(FB_O), 1);
     mbar_init(bar(FB_END), 1);
@@ -181,14 +188,8 @@ __global__ void __launch_bounds__(192, 2)
       auto wait_all = [&](uint32_t b, uint32_t par) {
         return __all_sync(0xffffffffu, mbar_wait(b, par, a.status));
       };
-      bool ok = wait_all(bar(FB_Q), 0);
-      for (int j = 0; ok && j < nblk; ++j) {
-        const int st = j & 1, u = j >> 1;
-        ok = wait_all(bar(FB_KF + st), u & 1);
-        // S/P columns are reused: the previous P V must have finished reading P.
-        if (ok && j > 0) ok = wait_all(bar(FB_O), (j - 1) & 1);
-        if (!ok || *abort_flag) break;
-        tc_fence_after();
+      auto issue_s = [&](int j) {  // S_j = Q K_j^T
+        const int st = j & 1;
 #pragma unroll
         for (int kk = 0; kk < D / 16; ++kk) {
           const uint32_t off = (uint32_t)(kk & 3) * 32u;  // 16 elements = 32 B within the slab
@@ -199,6 +200,23 @@ __global__ void __launch_bounds__(192, 2)
           mma_ss_p(tmem + C::COL_S, ad, bd, idesc_s, kk > 0 ? 1u : 0u, leader);
         }
         mma_commit_p(bar(FB_S), leader);
+      };
+      bool ok = wait_all(bar(FB_Q), 0) && wait_all(bar(FB_KF), 0);
+      if (ok && !*abort_flag) {
+        tc_fence_after();
+        issue_s(0);
+      }
+      for (int j = 0; ok && j < nblk; ++j) {
+        const int st = j & 1, u = j >> 1;
+        // S_{j+1} as soon as the softmax warps hold S_j in registers: it is computed while they
+        // work on block j (P_j goes to its own columns, so S_{j+1} need not wait for P_j V_j).
+        if (j + 1 < nblk) {
+          ok = wait_all(bar(FB_KF + (st ^ 1)), ((j + 1) >> 1) & 1);
+          if (ok) ok = wait_all(bar(FB_SC), j & 1);
+          if (!ok || *abort_flag) break;
+          tc_fence_after();
+          issue_s(j + 1);
+        }
         ok = wait_all(bar(FB_VF + st), u & 1);
         if (ok) ok = wait_all(bar(FB_P), j & 1);
         if (!ok || *abort_flag) break;
@@ -207,7 +225,7 @@ __global__ void __launch_bounds__(192, 2)
         for (int kk = 0; kk < C::BN / 16; ++kk) {
           const uint64_t bd = sdesc_sw128(sbase + C::OFF_V + st * C::KV_BYTES + kk * 16 * 128,
                                           C::BN * 128, 1024);
-          mma_ts_p(tmem + C::COL_O, tmem + C::COL_S + kk * 8, bd, idesc_o,
+          mma_ts_p(tmem + C::COL_O, tmem + C::COL_P + kk * 8, bd, idesc_o,
                    (j > 0 || kk > 0) ? 1u : 0u, leader);
         }
         mma_commit_p(bar(FB_O), leader);
@@ -241,6 +259,8 @@ __global__ void __launch_bounds__(192, 2)
       tmem_ld_wait_only();
 #pragma unroll
       for (int c = 0; c < C::BN / 32; ++c) tmem_pin(sr[c]);
+      tc_fence_before();
+      mbar_arrive(bar(FB_SC));  // S_j is in registers: the MMA warp may write S_{j+1}
 
       const int n0 = j * C::BN;
       const bool full = (n0 + C::BN <= L) && (!p.causal || n0 + C::BN - 1 <= m0);
@@ -285,7 +305,7 @@ __global__ void __launch_bounds__(192, 2)
 #pragma unroll
           for (int i = 0; i < 32; i += 2) {
             const float2 pp = p_pair(__uint_as_float(sr[c][i]), __uint_as_float(sr[c][i + 1]),
-                                     ((i >> 1) & 3) < kEmuPairs);
+                                     ((i >> 1) & 3) < kEmuPairs<D>);
             rs2 = __fadd2_rn(rs2, pp);
             pk[c >> 1][(c & 1) * 16 + (i >> 1)] = pack2<BF16>(pp.x, pp.y);
           }
@@ -297,7 +317,7 @@ __global__ void __launch_bounds__(192, 2)
           for (int i = 0; i < 32; i += 2) {
             const int col = n0 + c * 32 + i;
             float2 pp = p_pair(__uint_as_float(sr[c][i]), __uint_as_float(sr[c][i + 1]),
-                               ((i >> 1) & 3) < kEmuPairs);
+                               ((i >> 1) & 3) < kEmuPairs<D>);
             pp.x = (col <= lim && row < L) ? pp.x : 0.f;
             pp.y = (col + 1 <= lim && row < L) ? pp.y : 0.f;
             rs2 = __fadd2_rn(rs2, pp);
@@ -307,8 +327,17 @@ __global__ void __launch_bounds__(192, 2)
       }
       const float rs = rs2.x + rs2.y;
       l_run = l_run * alpha + rs;
-      // O correction. PV_{j-1} completed before S_j's commit fired (commit tracks every
-      // earlier tcgen05 op of the issuing thread), so O is final for blocks < j here.
+      // P_{j-1} V_{j-1} must have retired before O is corrected and before P_j overwrites
+      // P_{j-1}; it was issued at the end of block j - 1, so this wait rarely blocks.
+      if (j > 0) {
+        bool okv = mbar_wait(bar(FB_O), (j - 1) & 1, a.status);
+        if (!__all_sync(0xffffffffu, okv)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+      }
+      // O correction: O is final for blocks < j here.
       if (__any_sync(0xffffffffu, need && j > 0)) {
 #pragma unroll
         for (int c = 0; c < D / 32; ++c) {
@@ -321,7 +350,7 @@ __global__ void __launch_bounds__(192, 2)
         }
       }
 #pragma unroll
-      for (int c = 0; c < C::BN / 64; ++c) tmem_st32(t_lane + C::COL_S + c * 32, pk[c]);
+      for (int c = 0; c < C::BN / 64; ++c) tmem_st32(t_lane + C::COL_P + c * 32, pk[c]);
       tmem_st_wait();
       tc_fence_before();
       mbar_arrive(bar(FB_P));

@@ -34,10 +34,10 @@ namespace sm100 {
 
 constexpr float kRescaleThreshold = 8.0f;
 // Element pairs, of every 4, whose exponential is evaluated on the FMA pipe (exp2_poly2).
-// Measured on B200: D = 128 gains from 2 of 4; at D = 64 the softmax is not bound by the
-// special-function unit and the extra FMA-pipe work only costs time.
+// Measured on B200: D = 128 gains from 1 of 4 (2 of 4 and more lose again); at D = 64 the
+// softmax is not bound by the special-function unit alone and the extra work only costs time.
 template <int D>
-constexpr int kEmuPairs = D == 128 ? 2 : 0;
+constexpr int kEmuPairs = D == 128 ? 1 : 0;
 
 template <int D>
 struct FwdCfg {

@@ -9,6 +9,7 @@
 #include <cstdio>
 #include <cstring>
 #include <mutex>
+#include <unordered_map>
 
 #include "ssa_internal.h"
 #include "ssa_tmap.h"
@@ -174,6 +175,23 @@ int bind_device(const void* ptr, const char* name) {
     cudaGetLastError();
     return fail(SSA_ERR_CUDA, "%s: cannot make device %d current", name, at.device);
   }
+  return SSA_OK;
+}
+
+int set_smem_limit_once(const void* func, int bytes) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return SSA_ERR_CUDA;
+  static std::mutex mu;
+  static std::unordered_map<const void*, int> done[kMaxDevices];  // bytes already granted
+  std::lock_guard<std::mutex> lk(mu);
+  auto it = done[dev].find(func);
+  if (it != done[dev].end() && it->second >= bytes) return SSA_OK;
+  if (cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes) !=
+      cudaSuccess) {
+    cudaGetLastError();
+    return SSA_ERR_CUDA;
+  }
+  done[dev][func] = bytes;
   return SSA_OK;
 }
 

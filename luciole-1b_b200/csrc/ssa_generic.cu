@@ -387,8 +387,7 @@ int run_fwd_generic(const Problem& p, TensorRef q, TensorRef k, TensorRef v, Ten
   constexpr int DP = D + 1;
   const size_t smem = sizeof(float) * (size_t)(kBM * DP + 2 * kBN * DP + kBM * (kBN + 1));
   auto kern = fwd_generic_kernel<T, D>;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) !=
-      cudaSuccess)
+  if (set_smem_limit_once(reinterpret_cast<const void*>(kern), (int)smem) != SSA_OK)
     return SSA_ERR_CUDA;
   dim3 grid((p.max_seqlen + kBM - 1) / kBM, p.B * p.Hq);
   kern<<<grid, kNT, smem, st>>>(p, q, k, v, o, lse);
@@ -406,10 +405,8 @@ int run_bwd_generic(const Problem& p, TensorRef q, TensorRef k, TensorRef v, Ten
   const size_t smem_q = sizeof(float) * (size_t)(2 * kBM * DP + 2 * kBN * DP + kBM * (kBN + 1));
   auto kkv = bwd_dkdv_generic_kernel<T, D>;
   auto kq = bwd_dq_generic_kernel<T, D>;
-  if (cudaFuncSetAttribute(kkv, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_kv) !=
-          cudaSuccess ||
-      cudaFuncSetAttribute(kq, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_q) !=
-          cudaSuccess)
+  if (set_smem_limit_once(reinterpret_cast<const void*>(kkv), (int)smem_kv) != SSA_OK ||
+      set_smem_limit_once(reinterpret_cast<const void*>(kq), (int)smem_q) != SSA_OK)
     return SSA_ERR_CUDA;
   dim3 gkv(ntiles, p.B * p.Hkv);
   kkv<<<gkv, kNT, smem_kv, st>>>(p, q, k, v, dout, lse, delta, dk, dv, dn_part, db_part, ntiles);

@@ -43,6 +43,10 @@ void note_launches(int n);
 int abi_validate_problem(const ssa_problem_t* pr);
 Problem abi_to_problem(const ssa_problem_t* pr);
 int abi_error(int code, const char* fmt, ...);
+// Raises `func`'s dynamic shared-memory limit to `bytes` once per device (the attribute lives in
+// the context), so later launches, including launches under CUDA stream capture, make no
+// attribute call. SSA_OK or SSA_ERR_CUDA.
+int set_smem_limit_once(const void* func, int bytes);
 // Makes the device owning `ptr` current on the calling thread (see ssa_capi.cu).
 int abi_bind_device(const void* ptr, const char* name);
 

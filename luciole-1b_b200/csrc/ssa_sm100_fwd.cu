@@ -414,8 +414,7 @@ int run_fwd(const Problem& p, TensorRef q, TensorRef k, TensorRef v, TensorRef o
   a.status = device_status_ptr();
   a.tiles_m = (p.max_seqlen + C::BM - 1) / C::BM;
   auto kern = fwd_sm100_kernel<D, BF16>;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           (int)C::SMEM_BYTES) != cudaSuccess)
+  if (set_smem_limit_once(reinterpret_cast<const void*>(kern), (int)C::SMEM_BYTES) != SSA_OK)
     return SSA_ERR_CUDA;
   const long long grid = (long long)a.tiles_m * p.B * p.Hq;
   kern<<<(unsigned)grid, C::THREADS, C::SMEM_BYTES, st>>>(tq, tk, tv, a);

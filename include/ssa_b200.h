@@ -12,6 +12,7 @@
  *   - Packed documents ("varlen"): pass cu_seqlens (int32, device, ndoc+1 entries) and
  *     B = ndoc; every tensor is then [T, H, D] given as {sB = 0, sH, sN} with N = T (total
  *     tokens) and max_seqlen = the longest document. lse / delta are [H, T] in that mode.
+ *     Padded packing (documents separated by padding rows) adds cu_seqlens_padded.
  *   - ssa_n is a device pointer to 1 float (reference: 0-d tensor, ssa_triton_attention.py:101)
  *     or to Hq floats (per-head n) when n_per_head != 0; ssa_b is a device pointer to 1 float.
  *     Both are read on the device, so no host synchronisation happens.
@@ -62,6 +63,11 @@ typedef struct {
   const float* ssa_b;   /* device, 1 float */
   const int32_t* cu_seqlens; /* device, B+1 entries, or NULL for dense [B,H,N,D] */
   int32_t max_seqlen;        /* longest document when cu_seqlens != NULL */
+  /* Optional (packed mode only): device, B+1 entries, the row where each document starts when
+   * documents are padded in the packed tensor (Megatron PackedSeqParams.cu_seqlens_q_padded).
+   * Document z then occupies rows [cu_seqlens_padded[z], + cu_seqlens[z+1] - cu_seqlens[z]);
+   * rows between documents are not read and not written. NULL: documents are contiguous. */
+  const int32_t* cu_seqlens_padded;
 } ssa_problem_t;
 
 /* Forward. Replaces ssa_flash_attn_forward (ssa_triton_kernel.py:732-792) and the

@@ -46,7 +46,7 @@ class SsaProblem(ctypes.Structure):
                 ("causal", ctypes.c_int32), ("softmax_scale", ctypes.c_float),
                 ("ssa_n", ctypes.c_void_p), ("n_per_head", ctypes.c_int32),
                 ("ssa_b", ctypes.c_void_p), ("cu_seqlens", ctypes.c_void_p),
-                ("max_seqlen", ctypes.c_int32)]
+                ("max_seqlen", ctypes.c_int32), ("cu_seqlens_padded", ctypes.c_void_p)]
 
 
 class SSAKernelError(RuntimeError):

@@ -69,15 +69,18 @@ def ssa_flash_attention(q, k, v, softmax_scale, ssa_n, ssa_b, causal=True, dropo
 
 
 class SSAVarlenFlashAttnFunc(Function):
-    """Packed-document SSA attention: q [T, Hq, D], k/v [T, Hkv, D], cu_seqlens int32."""
+    """Packed-document SSA attention: q [T, Hq, D], k/v [T, Hkv, D], cu_seqlens int32, and
+    optionally cu_seqlens_padded (start row of each document when padding separates them)."""
 
     @staticmethod
-    def forward(ctx, q, k, v, cu_seqlens, max_seqlen, softmax_scale, ssa_n, ssa_b, causal):
+    def forward(ctx, q, k, v, cu_seqlens, max_seqlen, softmax_scale, ssa_n, ssa_b, causal,
+                cu_seqlens_padded=None):
         ssa_n_f32 = ssa_n.float().contiguous()
         ssa_b_f32 = ssa_b.float().contiguous()
         out, lse = ssa_flash_attn_varlen_forward(q, k, v, cu_seqlens, max_seqlen, softmax_scale,
-                                                 ssa_n_f32, ssa_b_f32, causal)
-        ctx.save_for_backward(q, k, v, out, lse, cu_seqlens, ssa_n_f32, ssa_b_f32)
+                                                 ssa_n_f32, ssa_b_f32, causal, cu_seqlens_padded)
+        ctx.save_for_backward(q, k, v, out, lse, cu_seqlens, ssa_n_f32, ssa_b_f32,
+                              cu_seqlens_padded)
         ctx.max_seqlen = max_seqlen
         ctx.softmax_scale = softmax_scale
         ctx.causal = causal
@@ -87,17 +90,19 @@ class SSAVarlenFlashAttnFunc(Function):
 
     @staticmethod
     def backward(ctx, dout):
-        q, k, v, out, lse, cu, n32, b32 = ctx.saved_tensors
+        q, k, v, out, lse, cu, n32, b32, cu_pad = ctx.saved_tensors
         dq, dk, dv, dn, db = ssa_flash_attn_varlen_backward(
-            q, k, v, out, dout.contiguous(), lse, cu, ctx.max_seqlen, ctx.softmax_scale, n32, b32,
-            ctx.causal)
+            q, k, v, out, dout, lse, cu, ctx.max_seqlen, ctx.softmax_scale, n32, b32,
+            ctx.causal, cu_pad)
         dn = dn.reshape(ctx.n_meta[0]).to(ctx.n_meta[1])
         db = db.reshape(ctx.b_meta[0]).to(ctx.b_meta[1])
-        return dq, dk, dv, None, None, None, dn, db, None
+        return dq, dk, dv, None, None, None, dn, db, None, None
 
 
 def ssa_flash_attn_varlen_func(q, k, v, cu_seqlens, max_seqlen, softmax_scale, ssa_n, ssa_b,
-                               causal=True):
-    """Packed documents (THD + cu_seqlens); each document attends only within itself."""
+                               causal=True, cu_seqlens_padded=None):
+    """Packed documents (THD + cu_seqlens); each document attends only within itself. With
+    cu_seqlens_padded, document z starts at row cu_seqlens_padded[z] (Megatron's
+    PackedSeqParams.cu_seqlens_q_padded) and padding rows get zero output and gradient."""
     return SSAVarlenFlashAttnFunc.apply(q, k, v, cu_seqlens, int(max_seqlen), softmax_scale,
-                                        ssa_n, ssa_b, causal)
+                                        ssa_n, ssa_b, causal, cu_seqlens_padded)

@@ -91,6 +91,13 @@ class SSAAttentionConfig:
         self.sequence_parallel = sequence_parallel
 
 
+def _same(a: Optional[Tensor], b: Tensor) -> bool:
+    """a is absent, the same storage as b, or equal to b."""
+    if a is None or a is b or (a.data_ptr() == b.data_ptr() and a.shape == b.shape):
+        return True
+    return torch.equal(a.to(b.dtype), b)
+
+
 def _megatron_to_kernel_view(t: Tensor) -> Tensor:
     """[S, B, H, D] -> [B, H, S, D] (zero-copy permute; the kernels take arbitrary strides)."""
     return t.permute(1, 2, 0, 3)
@@ -201,15 +208,26 @@ class SSATritonAttention(MegatronModule):
         return context.reshape(*context.size()[:-2], self.hidden_size_per_partition)
 
     def _forward_packed(self, query, key, value, ssa_n, ssa_b, is_causal, psp):
-        """THD packed sequences: query [T, 1, np, hn] or [T, np, hn] with cu_seqlens_q."""
+        """THD packed sequences: query [T, 1, np, hn] or [T, np, hn] with Megatron's
+        PackedSeqParams: cu_seqlens_q (document lengths), optionally cu_seqlens_q_padded
+        (document start rows when the packer pads each document, as NeMo's packed datasets do
+        for context parallelism: training/finetune/nemo_patch/data/core.py:874-999) and
+        max_seqlen_q. Padding rows get zero output and zero gradient."""
         cu = getattr(psp, "cu_seqlens_q", None)
         if cu is None:
             raise ValueError("packed_seq_params needs cu_seqlens_q")
+        # Same-tensor checks first: comparing contents synchronises with the device.
         cu_kv = getattr(psp, "cu_seqlens_kv", None)
-        if cu_kv is not None and not torch.equal(cu_kv, cu):
+        if not _same(cu_kv, cu):
             raise ValueError("self-attention packing needs cu_seqlens_kv == cu_seqlens_q")
-        max_s = getattr(psp, "max_seqlen_q", None)
         cu = cu.to(torch.int32)
+        cu_pad = getattr(psp, "cu_seqlens_q_padded", None)
+        if cu_pad is not None:
+            if not _same(getattr(psp, "cu_seqlens_kv_padded", None), cu_pad):
+                raise ValueError("self-attention packing needs cu_seqlens_kv_padded == "
+                                 "cu_seqlens_q_padded")
+            cu_pad = cu_pad.to(torch.int32)
+        max_s = getattr(psp, "max_seqlen_q", None)
         if max_s is None:
             max_s = int((cu[1:] - cu[:-1]).max().item())
         squeeze = query.dim() == 4
@@ -217,7 +235,7 @@ class SSATritonAttention(MegatronModule):
         k3 = key.squeeze(1) if squeeze else key
         v3 = value.squeeze(1) if squeeze else value
         out = ssa_flash_attn_varlen_func(q3, k3, v3, cu, int(max_s), self.softmax_scale, ssa_n,
-                                         ssa_b, is_causal)
+                                         ssa_b, is_causal, cu_pad)
         if self.training and self.dropout_p > 0:
             out = self.attention_dropout(out)
         out = out.reshape(out.shape[0], self.hidden_size_per_partition)

@@ -48,14 +48,16 @@ def _params(ssa_n: torch.Tensor, ssa_b: torch.Tensor, hq: int, device) -> Tuple[
 
 def _problem(q: torch.Tensor, hkv: int, softmax_scale: float, n: torch.Tensor, b: torch.Tensor,
              per_head: int, causal: bool, B: int, N: int,
-             cu_seqlens: Optional[torch.Tensor] = None, max_seqlen: int = 0) -> _lib.SsaProblem:
+             cu_seqlens: Optional[torch.Tensor] = None, max_seqlen: int = 0,
+             cu_seqlens_padded: Optional[torch.Tensor] = None) -> _lib.SsaProblem:
     if q.dtype not in _lib.DTYPE_CODES:
         raise ValueError(f"unsupported dtype {q.dtype}")
     hq, d = q.shape[1], q.shape[-1]
     return _lib.SsaProblem(
         _lib.DTYPE_CODES[q.dtype], B, hq, hkv, N, d, 1 if causal else 0, float(softmax_scale),
         n.data_ptr(), per_head, b.data_ptr(),
-        cu_seqlens.data_ptr() if cu_seqlens is not None else None, int(max_seqlen))
+        cu_seqlens.data_ptr() if cu_seqlens is not None else None, int(max_seqlen),
+        cu_seqlens_padded.data_ptr() if cu_seqlens_padded is not None else None)
 
 
 def _tma_ok(t: torch.Tensor) -> bool:
@@ -167,6 +169,15 @@ def _check_thd(q, k, v, cu_seqlens):
     return T, Hq, k.shape[1], D, cu_seqlens.numel() - 1
 
 
+def _check_padded(cu_seqlens, cu_seqlens_padded):
+    if cu_seqlens_padded is None:
+        return None
+    if (cu_seqlens_padded.dtype != torch.int32 or cu_seqlens_padded.shape != cu_seqlens.shape
+            or not cu_seqlens_padded.is_cuda):
+        raise ValueError("cu_seqlens_padded must be a CUDA int32 tensor shaped like cu_seqlens")
+    return cu_seqlens_padded
+
+
 def _prep3(t, fam):
     if t.stride(-1) != 1 or (fam == 1 and not _tma_ok(t)):
         return t.contiguous()
@@ -174,22 +185,25 @@ def _prep3(t, fam):
 
 
 def ssa_flash_attn_varlen_forward(q, k, v, cu_seqlens, max_seqlen, softmax_scale, ssa_n, ssa_b,
-                                  causal=True):
+                                  causal=True, cu_seqlens_padded=None):
     """Packed documents: q [T, Hq, D], k/v [T, Hkv, D], cu_seqlens int32 [ndoc+1].
 
     Each document attends only within itself (causal or not). Returns (out [T, Hq, D],
-    lse [Hq, T] fp32). No reference counterpart: the reference asserts packed sequences off
+    lse [Hq, T] fp32). With cu_seqlens_padded (Megatron's cu_seqlens_q_padded), document z
+    starts at row cu_seqlens_padded[z] and the padding rows between documents are ignored; their
+    output rows are zero. No reference counterpart: the reference asserts packed sequences off
     (ssa_triton_attention.py:154-156).
     """
     lib = _lib.load()
     T, Hq, Hkv, D, ndoc = _check_thd(q, k, v, cu_seqlens)
+    cu_pad = _check_padded(cu_seqlens, cu_seqlens_padded)
     n, b, per_head = _params(ssa_n, ssa_b, Hq, q.device)
-    prob = _lib.SsaProblem(_lib.DTYPE_CODES[q.dtype], ndoc, Hq, Hkv, T, D, 1 if causal else 0,
-                           float(softmax_scale), n.data_ptr(), per_head, b.data_ptr(),
-                           cu_seqlens.data_ptr(), int(max_seqlen))
+    prob = _problem(q, Hkv, softmax_scale, n, b, per_head, causal, ndoc, T,
+                    cu_seqlens, max_seqlen, cu_pad)
     fam = lib.ssa_attn_kernel_family(ctypes.byref(prob))
     q, k, v = _prep3(q, fam), _prep3(k, fam), _prep3(v, fam)
-    out = torch.empty(q.shape, dtype=q.dtype, device=q.device)
+    alloc = torch.zeros if cu_pad is not None else torch.empty
+    out = alloc(q.shape, dtype=q.dtype, device=q.device)
     lse = torch.empty((Hq, T), device=q.device, dtype=torch.float32)
     with torch.cuda.device(q.device):
         rc = lib.ssa_attn_fwd(ctypes.byref(prob), _lib.tensor_thd(q), _lib.tensor_thd(k),
@@ -200,20 +214,23 @@ def ssa_flash_attn_varlen_forward(q, k, v, cu_seqlens, max_seqlen, softmax_scale
 
 
 def ssa_flash_attn_varlen_backward(q, k, v, out, dout, lse, cu_seqlens, max_seqlen,
-                                   softmax_scale, ssa_n, ssa_b, causal=True):
-    """Backward of :func:`ssa_flash_attn_varlen_forward`. Returns (dq, dk, dv, dn, db)."""
+                                   softmax_scale, ssa_n, ssa_b, causal=True,
+                                   cu_seqlens_padded=None):
+    """Backward of :func:`ssa_flash_attn_varlen_forward`. Returns (dq, dk, dv, dn, db); with
+    cu_seqlens_padded the gradient rows of padding tokens are zero."""
     lib = _lib.load()
     T, Hq, Hkv, D, ndoc = _check_thd(q, k, v, cu_seqlens)
+    cu_pad = _check_padded(cu_seqlens, cu_seqlens_padded)
     n, b, per_head = _params(ssa_n, ssa_b, Hq, q.device)
-    prob = _lib.SsaProblem(_lib.DTYPE_CODES[q.dtype], ndoc, Hq, Hkv, T, D, 1 if causal else 0,
-                           float(softmax_scale), n.data_ptr(), per_head, b.data_ptr(),
-                           cu_seqlens.data_ptr(), int(max_seqlen))
+    prob = _problem(q, Hkv, softmax_scale, n, b, per_head, causal, ndoc, T,
+                    cu_seqlens, max_seqlen, cu_pad)
     fam = lib.ssa_attn_kernel_family(ctypes.byref(prob))
     q, k, v, dout = _prep3(q, fam), _prep3(k, fam), _prep3(v, fam), _prep3(dout, fam)
     out = out if out.stride(-1) == 1 else out.contiguous()
-    dq = torch.empty(q.shape, dtype=q.dtype, device=q.device)
-    dk = torch.empty(k.shape, dtype=k.dtype, device=k.device)
-    dv = torch.empty(v.shape, dtype=v.dtype, device=v.device)
+    alloc = torch.zeros if cu_pad is not None else torch.empty
+    dq = alloc(q.shape, dtype=q.dtype, device=q.device)
+    dk = alloc(k.shape, dtype=k.dtype, device=k.device)
+    dv = alloc(v.shape, dtype=v.dtype, device=v.device)
     dn = torch.empty(n.shape, device=q.device, dtype=torch.float32)
     db = torch.empty((), device=q.device, dtype=torch.float32)
     ws_bytes = lib.ssa_attn_bwd_workspace_size(ctypes.byref(prob))

@@ -51,6 +51,8 @@ int check_problem(const ssa_problem_t* pr) {
   if (!generic_supports_head_dim(pr->D))
     return fail(SSA_ERR_UNSUPPORTED, "head dim D=%d not supported (16, 32, 64, 128)", pr->D);
   if (!pr->ssa_n || !pr->ssa_b) return fail(SSA_ERR_NULL, "ssa_n / ssa_b device pointer is NULL");
+  if (!pr->cu_seqlens && pr->cu_seqlens_padded)
+    return fail(SSA_ERR_BAD_SHAPE, "cu_seqlens_padded needs cu_seqlens (packed mode)");
   if (pr->cu_seqlens && pr->max_seqlen <= 0)
     return fail(SSA_ERR_BAD_SHAPE, "varlen needs max_seqlen > 0");
   if (!(pr->softmax_scale == pr->softmax_scale))
@@ -79,6 +81,7 @@ Problem to_problem(const ssa_problem_t* pr) {
   p.n_per_head = pr->n_per_head ? 1 : 0;
   p.b_ptr = pr->ssa_b;
   p.cu_seqlens = pr->cu_seqlens;
+  p.cu_seqlens_padded = pr->cu_seqlens ? pr->cu_seqlens_padded : nullptr;
   p.max_seqlen = pr->cu_seqlens ? pr->max_seqlen : pr->N;
   return p;
 }

@@ -33,8 +33,9 @@ struct Problem {
   const float* n_ptr;
   int n_per_head;
   const float* b_ptr;
-  const int* cu_seqlens;  // nullptr: dense
-  int max_seqlen;         // rows a sequence can have (N when dense)
+  const int* cu_seqlens;         // nullptr: dense
+  const int* cu_seqlens_padded;  // packed with padding: start row of each document, or nullptr
+  int max_seqlen;                // rows a sequence can have (N when dense)
 };
 
 struct TensorRef {
@@ -45,8 +46,9 @@ struct TensorRef {
 // Start row and length of sequence z (a batch entry, or a document when varlen).
 __device__ __forceinline__ void seq_bounds(const Problem& p, int z, int& start, int& len) {
   if (p.cu_seqlens) {
-    start = __ldg(p.cu_seqlens + z);
-    len = __ldg(p.cu_seqlens + z + 1) - start;
+    const int c0 = __ldg(p.cu_seqlens + z);
+    len = __ldg(p.cu_seqlens + z + 1) - c0;
+    start = p.cu_seqlens_padded ? __ldg(p.cu_seqlens_padded + z) : c0;
   } else {
     start = 0;
     len = p.N;

@@ -71,7 +71,8 @@ def test_bad_problems_rejected_before_any_cuda_call(lib):
              (_prob(dtype=7), _lib.SSA_ERR_UNSUPPORTED, b"dtype"),
              (_prob(N=0), _lib.SSA_ERR_BAD_SHAPE, b"non-positive"),
              (_prob(ssa_n=None), _lib.SSA_ERR_NULL, b"ssa_n"),
-             (_prob(cu_seqlens=64, max_seqlen=0), _lib.SSA_ERR_BAD_SHAPE, b"max_seqlen")]
+             (_prob(cu_seqlens=64, max_seqlen=0), _lib.SSA_ERR_BAD_SHAPE, b"max_seqlen"),
+             (_prob(cu_seqlens_padded=64), _lib.SSA_ERR_BAD_SHAPE, b"cu_seqlens_padded")]
     for prob, code, msg in cases:
         rc = lib.ssa_attn_fwd(ctypes.byref(prob), t, t, t, t, 16, None, 0, None)
         assert rc == code, (rc, code)

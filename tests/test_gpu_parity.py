@@ -269,6 +269,68 @@ def test_varlen_packed_documents(D, dtype, cuda_device):
     assert_scalar_close("db", db, ref["db"])
 
 
+@pytest.mark.parametrize("D,dtype", [(64, torch.bfloat16), (128, torch.bfloat16),
+                                     (64, torch.float32)])
+def test_varlen_padded_packing(D, dtype, cuda_device):
+    """Megatron PackedSeqParams with cu_seqlens_q_padded: documents separated by padding rows
+    (NeMo's packed datasets, training/finetune/nemo_patch/data/core.py:874-999). Padding rows,
+    filled with large values here, must not influence any document, and their output and
+    gradient rows must be zero."""
+    from types import SimpleNamespace
+    from SSA.ssa_triton_attention import SSAAttentionConfig, SSATritonAttention
+    lens, pads = [100, 257, 31, 200], [12, 0, 33, 7]
+    Hq, Hkv = 8, 2
+    starts = [0]
+    for ln, pd in zip(lens, pads):
+        starts.append(starts[-1] + ln + pd)
+    T = starts[-1]
+    cu = torch.tensor([0] + list(torch.tensor(lens).cumsum(0)), dtype=torch.int32)
+    cu_pad = torch.tensor(starts, dtype=torch.int32)
+    valid = torch.zeros(T, dtype=torch.bool)
+    for st, ln in zip(starts[:-1], lens):
+        valid[st:st + ln] = True
+    g = torch.Generator().manual_seed(81)
+
+    def filled(h, scale):
+        x = torch.randn(T, h, D, generator=g) * scale
+        x[~valid] = 30.0  # padding garbage
+        return x.to(dtype)
+
+    q, k, v, do = filled(Hq, 0.5), filled(Hkv, 0.5), filled(Hkv, 0.5), filled(Hq, 1.0)
+    n, b = torch.tensor(0.55), torch.tensor(0.8)
+    dev = cuda_device
+    qd, kd, vd, dod = (t.to(dev).requires_grad_(True) if i < 3 else t.to(dev)
+                       for i, t in enumerate((q, k, v, do)))
+    from SSA.ssa_flash_attention import ssa_flash_attn_varlen_func
+    nd = n.to(dev).requires_grad_(True)
+    out = ssa_flash_attn_varlen_func(qd, kd, vd, cu.to(dev), max(lens), D ** -0.5, nd, b.to(dev),
+                                     True, cu_pad.to(dev))
+    out.backward(dod)
+    torch.cuda.synchronize()
+    ref = ssa_reference_grads_varlen(q[valid], k[valid], v[valid], cu, D ** -0.5, n, b, do[valid],
+                                     True)
+    got = dict(out=out.detach(), dq=qd.grad, dk=kd.grad, dv=vd.grad)
+    for name in ("out", "dq", "dk", "dv"):
+        x = got[name].cpu()
+        assert (x[~valid] == 0).all(), f"{name}: padding rows not zero"
+        if dtype == torch.float32:
+            assert max_rel(x[valid], ref[name]) <= 1e-5, name
+        else:
+            assert_lowp_close(name, x[valid], ref[name])
+    assert_scalar_close("dn", nd.grad, ref["dn"])
+    # the module takes the same layout through packed_seq_params
+    cfg = SSAAttentionConfig(num_attention_heads=Hq, kv_channels=D, num_query_groups=Hkv)
+    mod = SSATritonAttention(cfg, layer_number=1, ssa_n=0.55, ssa_b=0.8).to(dev)
+    psp = SimpleNamespace(cu_seqlens_q=cu.to(dev), cu_seqlens_kv=None,
+                          cu_seqlens_q_padded=cu_pad.to(dev), cu_seqlens_kv_padded=None,
+                          max_seqlen_q=max(lens))
+    ctx = mod(q.to(dev).unsqueeze(1), k.to(dev).unsqueeze(1), v.to(dev).unsqueeze(1), None,
+              packed_seq_params=psp)
+    torch.cuda.synchronize()
+    assert ctx.shape == (T, 1, Hq * D)
+    assert torch.equal(ctx.reshape(T, Hq, D), out.detach())
+
+
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
 def test_bit_deterministic(dtype, cuda_device):
     """Two identical runs are bit-identical (check_ssa_triton_parity.py:507-562, atol 0).

@@ -262,6 +262,104 @@ def _one_ref_step(threads):
     return fl / el / 1e12, el, fl, 1
 
 
+def run_train(args):
+    """one Luciole-1B-shaped training step per timed step (forward, loss,
+    backward with DDP's gradient all-reduce, AdamW on fp32 masters) on random token ids,
+    sequence 2048, micro-batch 4 per GPU. value = tokens/s of the whole job."""
+    import luciole_train as LT
+    from SSA import _lib
+    world, rank, local = dist_setup(args)
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    cfg = LT.LucioleConfig()
+    mbs, seq = 4, 2048
+    model = LT.build(cfg, dev, torch.bfloat16, seed=0)
+    net = model
+    if world > 1:
+        from torch.nn.parallel import DistributedDataParallel as DDP
+        net = DDP(model, device_ids=[local], gradient_as_bucket_view=True)
+    opt = LT.MasterWeightAdamW(list(model.parameters()))
+    g = torch.Generator().manual_seed(1000 + rank)
+    tok_h = torch.randint(0, cfg.vocab, (mbs, seq + 1), generator=g).pin_memory()
+    tok = tok_h.to(dev)
+
+    def barrier():
+        if world > 1:
+            torch.distributed.barrier(device_ids=[local])
+        torch.cuda.synchronize(dev)
+
+    for _ in range(args.warmup):
+        LT.train_step(net, opt, tok[:, :-1], tok[:, 1:])
+    barrier()
+    steps = min(args.steps, 30)
+    st = torch.cuda.current_stream(dev)
+    launches0 = _lib.launch_count()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local) as clk:
+        barrier()
+        e0.record(st)
+        for _ in range(steps):
+            LT.train_step(net, opt, tok[:, :-1], tok[:, 1:])
+        e1.record(st)
+        barrier()
+    launches = _lib.launch_count() - launches0
+    ms = e0.elapsed_time(e1) / steps
+    # e2e: token ids copied from pinned host memory and the loss read back, every step
+    buf = torch.empty_like(tok)
+    loss_h = torch.empty((), dtype=torch.float32).pin_memory()
+    barrier()
+    e2, e3 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2e_steps = max(3, min(steps, 10))
+    e2.record(st)
+    for _ in range(e2e_steps):
+        buf.copy_(tok_h, non_blocking=True)
+        loss = LT.train_step(net, opt, buf[:, :-1], buf[:, 1:])
+        loss_h.copy_(loss, non_blocking=True)
+    e3.record(st)
+    barrier()
+    e2e_ms = e2.elapsed_time(e3) / e2e_steps
+    if world > 1:
+        t = torch.tensor([ms, e2e_ms], device=dev)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms, e2e_ms = (float(x) for x in t.tolist())
+    tokens = world * mbs * seq
+    value = tokens / (ms * 1e-3)
+    flops_tok = LT.train_flops_per_token(cfg, seq)
+    peak_tf, _, peak_kind = measured_peaks()
+    sustained = peak_tf
+    pk = REPO / "MEASURED_PEAKS.json"
+    if pk.exists():
+        sustained = json.loads(pk.read_text()).get("bf16_tflops_sustained", peak_tf)
+    achieved = flops_tok * tokens / world / (ms * 1e-3) / 1e12
+    if rank == 0:
+        line = {
+            "metric": "Luciole-1B train tokens/s (bf16 weights, fp32 master AdamW, seq 2048, "
+                      "mbs 4 per GPU)",
+            "value": value, "unit": "tokens/s", "n_gpus": world, "steps": steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "config5: Llama-style decoder 16 x 2048, 32/8 heads (D=64), "
+                                   "SwiGLU 5632, RMSNorm, RoPE 1e4, vocab 65536, SSA attention "
+                                   "kernels; random-init weights, uniform random token ids",
+                       "global_batch": mbs * world, "seq_len": seq,
+                       "params": LT.param_count(cfg),
+                       "parallelism": f"DDP x{world} (NCCL all-reduce of bf16 grads)"},
+            "e2e": {"value": tokens / (e2e_ms * 1e-3), "unit": "tokens/s",
+                    "h2d_bytes_per_step": tok_h.numel() * tok_h.element_size(),
+                    "d2h_bytes_per_step": 4, "ms_per_step": e2e_ms},
+            "roofline": {"bound": "tensor", "kernel": "whole training step (model FLOPs)",
+                         "achieved": achieved, "peak": sustained, "unit": "TFLOP/s",
+                         "frac": achieved / sustained,
+                         "peak_kind": f"{peak_kind} bf16 sustained", "traffic": None},
+            "cpu_baseline": None,
+            "clocks": clk.summary(),
+            "gpu_launches": launches,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        torch.distributed.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -269,12 +367,23 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--config", default="c2", choices=sorted(CONFIGS))
+    ap.add_argument("--config", default="c2", choices=sorted(CONFIGS) + ["c5"],
+                    help="c2 (headline), c3, c4: attention workloads; c5: the Luciole-1B "
+                         "training step (tokens/s)")
     ap.add_argument("--cp", action="store_true",
                     help="context-parallel ring over the ranks (strong scaling of one sequence; "
                          "use with --config c4 under torchrun)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    if args.config == "c5":
+        if args.impl == "reference":
+            if int(os.environ.get("RANK", "0")) == 0:
+                print(json.dumps({"impl": "reference", "unavailable": "the reference's training "
+                                  "step needs NeMo / Megatron and its Triton kernels on a GPU, "
+                                  "none of which is in this image"}), flush=True)
+            return
+        run_train(args)
+        return
     select_config(args.config)
     if args.impl == "reference":
         run_reference(args)

@@ -587,7 +587,9 @@ __global__ void __launch_bounds__(512, 1)
       }
     }
     if (!ok) *abort_flag = 1;
-    if (lane == 0) bulk_wait0();
+    // The staging buffers must outlive the TMA engine's reads of them; the reduce-adds' global
+    // writes need no wait here (they are performed before the grid completes).
+    if (lane == 0) bulk_wait_read0();
   }
 
   tc_fence_before();
@@ -1132,7 +1134,9 @@ __global__ void __launch_bounds__(512, 1)
       }
     }
     if (!ok) *abort_flag = 1;
-    if (lane == 0) bulk_wait0();
+    // The staging buffers must outlive the TMA engine's reads of them; the reduce-adds' global
+    // writes need no wait here (they are performed before the grid completes).
+    if (lane == 0) bulk_wait_read0();
   }
 
   tc_fence_before();

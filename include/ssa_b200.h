@@ -117,6 +117,13 @@ int ssa_attn_kernel_family(const ssa_problem_t* prob);
  * (synchronises `stream`). 0 = no error, else SSA_ERR_DEVICE_TIMEOUT. */
 int ssa_device_status(void* stream);
 
+/* Failure-path self-test: launches one kernel that waits on an mbarrier no thread completes,
+ * through the same bounded wait the attention kernels use but limited to wait_cycles; the
+ * expired wait records SSA_ERR_DEVICE_TIMEOUT in the device status word (read and clear it
+ * with ssa_device_status; until then the attention kernels skip their work). No fault, no
+ * trap. No reference counterpart. */
+int ssa_selftest_device_timeout(uint64_t wait_cycles, void* stream);
+
 /* Number of CUDA kernels this library has launched in this process (all devices, all
  * threads). Lets a caller count the device work behind a call without a profiler. */
 uint64_t ssa_kernel_launch_count(void);

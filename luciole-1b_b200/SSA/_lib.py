@@ -32,6 +32,7 @@ EXPORTED_SYMBOLS = (
     "ssa_attn_fwd", "ssa_attn_fwd_workspace_size", "ssa_attn_bwd_preprocess", "ssa_attn_bwd",
     "ssa_attn_bwd_workspace_size", "ssa_attn_kernel_family", "ssa_device_status",
     "ssa_last_error", "ssa_version", "ssa_kernel_launch_count", "ssa_attn_bwd_noalloc",
+    "ssa_selftest_device_timeout",
 )
 
 
@@ -91,6 +92,8 @@ def load() -> ctypes.CDLL:
         lib.ssa_attn_bwd_workspace_size.restype = sz
         lib.ssa_attn_kernel_family.argtypes = [P]
         lib.ssa_attn_kernel_family.restype = ctypes.c_int
+        lib.ssa_selftest_device_timeout.argtypes = [ctypes.c_uint64, vp]
+        lib.ssa_selftest_device_timeout.restype = ctypes.c_int
         lib.ssa_device_status.argtypes = [vp]
         lib.ssa_device_status.restype = ctypes.c_int
         lib.ssa_last_error.argtypes = []

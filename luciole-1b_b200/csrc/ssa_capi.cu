@@ -349,6 +349,19 @@ int ssa_attn_bwd(const ssa_problem_t* prob, ssa_tensor_t q, ssa_tensor_t k, ssa_
   return finish_launch(rc, "ssa_attn_bwd(dn/db reduce)");
 }
 
+int ssa_selftest_device_timeout(uint64_t wait_cycles, void* stream) {
+  int dev = -1;
+  if (cudaStreamGetDevice(static_cast<cudaStream_t>(stream), &dev) == cudaSuccess)
+    cudaSetDevice(dev);
+  else
+    cudaGetLastError();
+  unsigned int* ptr = device_status_ptr();
+  if (!ptr) return fail(SSA_ERR_CUDA, "cannot resolve the device status word");
+  return finish_launch(launch_selftest_timeout(ptr, (long long)wait_cycles,
+                                               static_cast<cudaStream_t>(stream)),
+                       "ssa_selftest_device_timeout");
+}
+
 int ssa_device_status(void* stream) {
   int dev = -1;
   if (cudaStreamGetDevice(static_cast<cudaStream_t>(stream), &dev) == cudaSuccess)

@@ -43,6 +43,9 @@ void note_launches(int n);
 int abi_validate_problem(const ssa_problem_t* pr);
 Problem abi_to_problem(const ssa_problem_t* pr);
 int abi_error(int code, const char* fmt, ...);
+// One CTA waiting on an mbarrier nobody completes, with a bounded wait of `cycles` (self-test of
+// the device-timeout path; ssa_sm100_fwd.cu).
+int launch_selftest_timeout(unsigned int* status, long long cycles, cudaStream_t st);
 // Raises `func`'s dynamic shared-memory limit to `bytes` once per device (the attribute lives in
 // the context), so later launches, including launches under CUDA stream capture, make no
 // attribute call. SSA_OK or SSA_ERR_CUDA.

@@ -54,13 +54,14 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
       : "memory");
   return ok != 0;
 }
-// Waits for the phase with the given parity to complete; false after ~kWaitCycles.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity,
-                                          unsigned int* status) {
+// Waits for the phase with the given parity to complete; false after ~limit cycles, with the
+// timeout recorded in the device status word.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, unsigned int* status,
+                                          long long limit = kWaitCycles) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   while (!mbar_try_wait(bar, parity)) {
-    if (clock64() - t0 > kWaitCycles) {
+    if (clock64() - t0 > limit) {
       atomicOr(status, 1u);
       return false;
     }

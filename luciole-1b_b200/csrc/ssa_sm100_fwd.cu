@@ -424,6 +424,28 @@ int run_fwd(const Problem& p, TensorRef q, TensorRef k, TensorRef v, TensorRef o
 
 }  // namespace sm100
 
+namespace sm100 {
+// Waits on an mbarrier that no thread arrives on: the bounded wait expires after `cycles` and
+// records the timeout in the status word, exactly as in the attention kernels.
+__global__ void selftest_timeout_kernel(unsigned int* status, long long cycles) {
+  __shared__ __align__(8) unsigned long long b;
+  const uint32_t bar = smem_u32(&b);
+  if (threadIdx.x == 0) {
+    mbar_init(bar, 1);
+    fence_mbar_init();
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) mbar_wait(bar, 0, status, cycles);
+}
+}  // namespace sm100
+
+int launch_selftest_timeout(unsigned int* status, long long cycles, cudaStream_t st) {
+  if (cycles < 0) return SSA_ERR_BAD_SHAPE;
+  sm100::selftest_timeout_kernel<<<1, 32, 0, st>>>(status, cycles);
+  note_launches(1);
+  return SSA_OK;
+}
+
 bool sm100_supports(int dtype, int D) {
   return (dtype == SSA_DTYPE_BF16 || dtype == SSA_DTYPE_F16) && (D == 64 || D == 128);
 }

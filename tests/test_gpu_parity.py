@@ -410,6 +410,29 @@ def test_config2_full_size_slice(cuda_device):
         assert torch.isfinite(t).all()
 
 
+def test_device_timeout_path_reports_and_recovers(cuda_device):
+    """Failure path without a GPU fault: a bounded wait that nothing completes (a 2M-cycle
+    limit, about a millisecond) must record SSA_ERR_DEVICE_TIMEOUT, the status read must clear
+    it, and the context must stay usable: an attention call afterwards computes normally."""
+    from SSA import _lib
+    lib = _lib.load()
+    st = _lib.stream_ptr(cuda_device)
+    assert lib.ssa_device_status(st) == _lib.SSA_OK
+    assert lib.ssa_selftest_device_timeout(2_000_000, st) == _lib.SSA_OK
+    assert lib.ssa_device_status(st) == _lib.SSA_ERR_DEVICE_TIMEOUT
+    assert lib.ssa_device_status(st) == _lib.SSA_OK  # cleared by the read
+    K = _api()
+    q = seeded((1, 2, 128, 64), 91, 0.5).to(cuda_device)
+    k = seeded((1, 2, 128, 64), 92, 0.5).to(cuda_device)
+    v = seeded((1, 2, 128, 64), 93, 0.5).to(cuda_device)
+    n, b = torch.tensor(0.7, device=cuda_device), torch.tensor(0.8, device=cuda_device)
+    out, _ = K.ssa_flash_attn_forward(q, k, v, 0.125, n, b, causal=True)
+    ref = ssa_reference_grads(q.cpu(), k.cpu(), v.cpu(), 0.125, n.cpu(), b.cpu(),
+                              torch.zeros(1, 2, 128, 64), True)
+    assert_lowp_close("out", out, ref["out"])
+    assert lib.ssa_device_status(st) == _lib.SSA_OK
+
+
 def test_device_status_clean(cuda_device):
     from SSA import _lib
     rc = _lib.load().ssa_device_status(_lib.stream_ptr(cuda_device))

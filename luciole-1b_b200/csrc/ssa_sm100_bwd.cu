@@ -891,38 +891,42 @@ __global__ void __launch_bounds__(512, 1)
       }
     } else if (warp == C::WARP_MMA) {
       // ------------------------------------------------------------ MMA issuer (converged)
-      const uint32_t leader = elect_one();
+      // The whole warp runs the schedule and its waits; one elected lane issues each batch.
+      // Descriptors are low words (constant high word) advanced by immediates (16-byte units).
+      const bool leader = elect_one() != 0;
       constexpr uint32_t id_s = idesc_f16(BF16, false, false, 128, 64);   // S^T, dP^T
       constexpr uint32_t id_g = idesc_f16(BF16, false, true, 128, 128);   // dV, dK (N = D)
       constexpr uint32_t id_q = idesc_f16(BF16, true, true, 128, 64);     // dQ^T
       const uint32_t sK = sbase + C::OFF_K, sV = sbase + C::OFF_V;
+      const uint32_t dK_s = sdesc_lo(sK, 16), dV_s = sdesc_lo(sV, 16);  // K-major K, V
+      const uint32_t dK_q = sdesc_lo(sK, C::KV_SLAB);                   // MN-major K (dQ^T's A)
       auto wait_all = [&](uint32_t b, uint32_t par) {
         return __all_sync(0xffffffffu, mbar_wait(b, par, a.status));
       };
       auto issue_sdp = [&](int t) {
+        if (!leader) return;
         const int st = t % C::STAGES;
-        const uint32_t qb = sbase + C::OFF_Q + st * C::QT_BYTES;
-        const uint32_t db = sbase + C::OFF_DO + st * C::QT_BYTES;
+        const uint32_t q_lo = sdesc_lo(sbase + C::OFF_Q + st * C::QT_BYTES, 16);
+        const uint32_t o_lo = sdesc_lo(sbase + C::OFF_DO + st * C::QT_BYTES, 16);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
-          const uint32_t sl = kk >> 2, off = (kk & 3) * 32;
-          mma_ss_p(tmem + C::COL_S, sdesc_sw128(sK + sl * C::KV_SLAB + off, 16, 1024),
-                   sdesc_sw128(qb + sl * C::QT_SLAB + off, 16, 1024), id_s, kk > 0 ? 1u : 0u,
-                   leader);
+          const uint32_t sl = kk >> 2, off = (kk & 3) * 2;
+          mma_ss_lo(tmem + C::COL_S, dK_s + sl * (C::KV_SLAB >> 4) + off,
+                    q_lo + sl * (C::QT_SLAB >> 4) + off, id_s, kk > 0);
         }
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
-          const uint32_t sl = kk >> 2, off = (kk & 3) * 32;
-          mma_ss_p(tmem + C::COL_DP, sdesc_sw128(sV + sl * C::KV_SLAB + off, 16, 1024),
-                   sdesc_sw128(db + sl * C::QT_SLAB + off, 16, 1024), id_s, kk > 0 ? 1u : 0u,
-                   leader);
+          const uint32_t sl = kk >> 2, off = (kk & 3) * 2;
+          mma_ss_lo(tmem + C::COL_DP, dV_s + sl * (C::KV_SLAB >> 4) + off,
+                    o_lo + sl * (C::QT_SLAB >> 4) + off, id_s, kk > 0);
         }
-        mma_commit_p(bar(B2_SF + (t & 1)), leader);
+        mma_commit(bar(B2_SF + (t & 1)));
       };
       bool ok = wait_all(bar(B2_KV), 0) && wait_all(bar(B2_QF), 0);
       if (ok) {
         tc_fence_after();
         issue_sdp(0);
+        __syncwarp();
       }
       for (int t = 0; ok && t < T; ++t) {
         const int st = t % C::STAGES, h = t & 1;
@@ -932,39 +936,47 @@ __global__ void __launch_bounds__(512, 1)
         if (!ok || *abort_flag) break;
         tc_fence_after();
         if (t + 1 < T) issue_sdp(t + 1);
+        __syncwarp();
         ok = wait_all(bar(B2_SM + h), (t >> 1) & 1);
         if (!ok || *abort_flag) break;
         tc_fence_after();
-        const uint32_t qb = sbase + C::OFF_Q + st * C::QT_BYTES;
-        const uint32_t db = sbase + C::OFF_DO + st * C::QT_BYTES;
-        const uint32_t ds = sbase + C::OFF_DS + h * C::DS_BYTES;
-        // dV += P^T dO (A: TMEM, K = 64 queries); dK += dS^T Q (A: shared dS^T, K-major)
+        if (leader) {
+          const uint32_t q_mn = sdesc_lo(sbase + C::OFF_Q + st * C::QT_BYTES, C::QT_SLAB);
+          const uint32_t o_mn = sdesc_lo(sbase + C::OFF_DO + st * C::QT_BYTES, C::QT_SLAB);
+          const uint32_t ds_k = sdesc_lo(sbase + C::OFF_DS + h * C::DS_BYTES, 16);
+          const uint32_t acc0 = t > 0 ? 1u : 0u;
+          // dV += P^T dO (A: TMEM, K = 64 queries); dK += dS^T Q (A: shared dS^T, K-major)
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          mma_ts_p(tmem + C::COL_DV, tmem + C::COL_PT + h * 32 + kk * 8,
-                   sdesc_sw128(db + kk * 2048, C::QT_SLAB, 1024), id_g, (t > 0 || kk > 0) ? 1u : 0u,
-                   leader);
+          for (int kk = 0; kk < 4; ++kk)
+            mma_ts_lo(tmem + C::COL_DV, tmem + C::COL_PT + h * 32 + kk * 8, o_mn + 128 * kk, id_g,
+                      kk > 0 ? 1u : acc0);
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk)
-          mma_ss_p(tmem + C::COL_DK, sdesc_sw128(ds + kk * 32, 16, 1024),
-                   sdesc_sw128(qb + kk * 2048, C::QT_SLAB, 1024), id_g, (t > 0 || kk > 0) ? 1u : 0u,
-                   leader);
-        mma_commit_p(bar(B2_BF + h), leader);
+          for (int kk = 0; kk < 4; ++kk)
+            mma_ss_lo(tmem + C::COL_DK, ds_k + 2 * kk, q_mn + 128 * kk, id_g, kk > 0 ? 1u : acc0);
+          mma_commit(bar(B2_BF + h));
+        }
+        __syncwarp();
         // dQ^T = K^T dS^T (A: K read MN-major, M = head dims; B: dS^T, N = queries)
         if (t >= 1) ok = wait_all(bar(B2_DQE), (t - 1) & 1);
         if (!ok) break;
         tc_fence_after();
+        if (leader) {
+          const uint32_t ds_mn = sdesc_lo(sbase + C::OFF_DS + h * C::DS_BYTES, 8192);
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          mma_ss_p(tmem + C::COL_DQ, sdesc_sw128(sK + kk * 2048, C::KV_SLAB, 1024),
-                   sdesc_sw128(ds + kk * 2048, 8192, 1024), id_q, kk > 0 ? 1u : 0u, leader);
-        mma_commit_p(bar(B2_DQF), leader);
-        mma_commit_p(bar(B2_DSF + h), leader);
-        mma_commit_p(bar(B2_QE + st), leader);
+          for (int kk = 0; kk < 8; ++kk)
+            mma_ss_lo(tmem + C::COL_DQ, dK_q + 128 * kk, ds_mn + 128 * kk, id_q, kk > 0);
+          mma_commit(bar(B2_DQF));
+          mma_commit(bar(B2_DSF + h));
+          mma_commit(bar(B2_QE + st));
+        }
+        __syncwarp();
       }
       if (!ok) *abort_flag = 1;
-      mma_commit_p(bar(B2_KVD), leader);
-      mma_commit_p(bar(B2_END), leader);
+      if (leader) {
+        mma_commit(bar(B2_KVD));
+        mma_commit(bar(B2_END));
+      }
+      __syncwarp();
       mbar_wait(bar(B2_END), 0, a.status);
     }
   } else if (warp < 8) {

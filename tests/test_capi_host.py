@@ -3,6 +3,8 @@ declares, sizes workspaces, rejects bad problems with the right status codes, an
 host layer (module shims, parameters, checkpoint keys) behaves like the reference's."""
 
 import ctypes
+import os
+import sys
 import re
 from pathlib import Path
 
@@ -136,3 +138,35 @@ def test_layer_spec_requires_megatron_only_when_called():
     except ImportError:
         with pytest.raises(ImportError):
             ls.get_ssa_triton_gpt_layer_spec()
+
+
+def test_missing_library_fails_loudly():
+    """No CPU or PyTorch fallback: without libssa_b200.so every entry point raises."""
+    import subprocess
+    code = ("import sys; sys.path[:0] = [%r, %r]\n"
+            "from SSA import _lib\n"
+            "try:\n    _lib.load()\nexcept RuntimeError as e:\n    print('raised', 'not found' in str(e))\n")
+    env = dict(os.environ, SSA_B200_LIB="/nonexistent/libssa_b200.so")
+    r = subprocess.run([sys.executable, "-c", code % (str(REPO), str(REPO / "luciole-1b_b200"))],
+                       capture_output=True, text=True, env=env, timeout=120)
+    assert r.stdout.strip() == "raised True", (r.stdout, r.stderr)
+
+
+def test_packed_params_validation_before_any_kernel():
+    """Megatron PackedSeqParams handling: mismatched kv boundaries and a missing cu_seqlens_q
+    are rejected on the host, without a device synchronisation when q / kv share storage."""
+    from types import SimpleNamespace
+    from SSA.ssa_triton_attention import SSAAttentionConfig, SSATritonAttention, _same
+    cfg = SSAAttentionConfig(num_attention_heads=4, kv_channels=64, num_query_groups=2)
+    mod = SSATritonAttention(cfg, layer_number=1)
+    q = torch.zeros(10, 1, 4, 64)
+    kv = torch.zeros(10, 1, 2, 64)
+    cu = torch.tensor([0, 4, 10], dtype=torch.int32)
+    with pytest.raises(ValueError, match="cu_seqlens_q"):
+        mod(q, kv, kv, None, packed_seq_params=SimpleNamespace(cu_seqlens_q=None))
+    bad = SimpleNamespace(cu_seqlens_q=cu, cu_seqlens_kv=torch.tensor([0, 5, 10], dtype=torch.int32),
+                          max_seqlen_q=6)
+    with pytest.raises(ValueError, match="cu_seqlens_kv"):
+        mod(q, kv, kv, None, packed_seq_params=bad)
+    assert _same(None, cu) and _same(cu, cu) and _same(cu.clone(), cu)
+    assert not _same(torch.tensor([0, 5, 10], dtype=torch.int32), cu)

@@ -445,7 +445,14 @@ __global__ void __launch_bounds__(512, 1)
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
         uint32_t pk[16], dk[16];
-        if (full)
+        // A chunk masked for every row of this warp (the lower part of a diagonal tile, or past
+        // the sequence end) has P = dS = 0: its transform is skipped.
+        const bool dead = !full && ((p.causal && mh + c * 32 + 31 < n0 + quad * 32) ||
+                                    mh + c * 32 >= L || n0 + quad * 32 >= L);
+        if (dead) {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) pk[i] = dk[i] = 0u;
+        } else if (full)
           bwd_chunk<32, BF16, false, true>(sx, dp, lrow + c * 32, drow + c * 32, n, cb, nbs,
                                            mh + c * 32, qmin, L, j < L, dn_acc, db_acc, pk, dk);
         else
@@ -1034,7 +1041,13 @@ __global__ void __launch_bounds__(512, 1)
         uint32_t pk[16], dk[16];
         const uint32_t(&cs)[32] = c ? s1 : s0;
         const uint32_t(&cd)[32] = c ? d1 : d0;
-        if (full)
+        // A chunk masked for every row of this warp: P = dS = 0, transform skipped.
+        const bool dead = !full && ((p.causal && mh + c * 32 + 31 < n0 + quad * 32) ||
+                                    mh + c * 32 >= L || n0 + quad * 32 >= L);
+        if (dead) {
+#pragma unroll
+          for (int i = 0; i < 16; ++i) pk[i] = dk[i] = 0u;
+        } else if (full)
           bwd_chunk<32, BF16, false, false>(cs, cd, lrow + c * 32, drow + c * 32, n, cb, nbs, mh + c * 32,
                                      qmin, L, j < L, dn_acc, db_acc, pk, dk);
         else

@@ -18,6 +18,8 @@
  *     Both are read on the device, so no host synchronisation happens.
  *   - lse is the base-2 normaliser M = log2(sum_j exp2(t_j * log2 e)), fp32, [B, Hq, N]
  *     contiguous (ssa_triton_kernel.py:248-255).
+ *   - Entry points that launch work first make the device owning the tensors current on the
+ *     calling thread (cudaSetDevice), so a thread that has not used CUDA yet works too.
  *   - All launches are asynchronous on `stream` (a cudaStream_t). Nothing here allocates
  *     device memory: scratch space is the caller's `workspace` (size from the *_workspace_size
  *     query). Entry points return an ssa_status_t; on error ssa_last_error() describes it.

@@ -62,12 +62,12 @@ def _cpu_worker(rank, world, port, q, k, v, do, n, b, scale, out_q):
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("per_head", [False, True])
-def test_ring_matches_full_sequence_cpu(per_head):
+@pytest.mark.parametrize("per_head,world", [(False, 2), (True, 2), (True, 4)])
+def test_ring_matches_full_sequence_cpu(per_head, world):
     from SSA.context_parallel import zigzag_gather
     from oracle.ssa_oracle import ssa_reference_grads
     g = torch.Generator().manual_seed(21)
-    B, Hq, Hkv, S, D, world = 1, 4, 2, 64, 8, 2
+    B, Hq, Hkv, S, D = 1, 4, 2, 64, 8
     q = torch.randn(B, Hq, S, D, generator=g, dtype=torch.float64)
     k = torch.randn(B, Hkv, S, D, generator=g, dtype=torch.float64)
     v = torch.randn(B, Hkv, S, D, generator=g, dtype=torch.float64)

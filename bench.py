@@ -404,7 +404,6 @@ def main():
     n = n_h.to(dev)
     bb = torch.tensor(SSA_B, device=dev)
     scale = D ** -0.5
-    red = torch.zeros(HQ + 1, device=dev)
     if DOC_LENS is not None:
         cu = torch.tensor([0] + list(torch.tensor(DOC_LENS).cumsum(0)), dtype=torch.int32,
                           device=dev)
@@ -447,7 +446,7 @@ def main():
         out, m = attn_fwd(q, k, v)
         dq, dk, dv, dn, db = attn_bwd(q, k, v, out, do, m)
         if reduce_params:
-            allreduce_ssa_param_grads(dn, db, buffer=red)
+            allreduce_ssa_param_grads(dn, db)
         return out, dq, dk, dv, dn, db
 
     def barrier():
@@ -465,6 +464,7 @@ def main():
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
            torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    pending = []
     with ClockSampler(local) as clk:
         barrier()
         start.record(st)
@@ -476,7 +476,10 @@ def main():
             dq, dk, dv, dn, db = attn_bwd(q, k, v, out, do, m)
             e2.record(st)
             if reduce_params:
-                allreduce_ssa_param_grads(dn, db, buffer=red)
+                # in place on the (adjacent) dn/db; overlaps the next step's forward
+                pending.append(allreduce_ssa_param_grads(dn, db, async_op=True))
+        for w in pending:  # every reduction finishes inside the timed region
+            w.wait()
         stop.record(st)
         barrier()
     launches = _lib.launch_count() - launches0
@@ -522,7 +525,7 @@ def main():
         out_, m_ = attn_fwd(qd, kd, vd)
         dq_, dk_, dv_, dn_, db_ = attn_bwd(qd, kd, vd, out_, dod, m_)
         if reduce_params:
-            allreduce_ssa_param_grads(dn_, db_, buffer=red)
+            allreduce_ssa_param_grads(dn_, db_)
         res = torch.cat([dn_.reshape(-1), db_.reshape(1)])
         ev = torch.cuda.Event()
         ev.record(st)

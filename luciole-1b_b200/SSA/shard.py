@@ -38,14 +38,25 @@ def batch_shard(B: int, world: int, rank: int) -> slice:
 
 
 def allreduce_ssa_param_grads(dn: torch.Tensor, db: torch.Tensor, group=None,
-                              buffer: Optional[torch.Tensor] = None):
+                              buffer: Optional[torch.Tensor] = None, async_op: bool = False):
     """Sum dn and db over the ranks of `group` with a single all-reduce (in place).
 
-    dn: 0-d or [Hq]; db: 0-d. `buffer` (numel >= dn.numel() + 1, same device) avoids an allocation.
-    Returns (dn, db).
+    dn: 0-d or [Hq]; db: 0-d. When dn and db are adjacent in one buffer (as the SSA backward
+    returns them), that buffer is reduced in place with no copies; otherwise they are packed into
+    `buffer` (numel >= dn.numel() + 1, same device; allocated when None) and unpacked after.
+    async_op=True (adjacent case only) returns the collective's Work without waiting: the caller
+    waits on it before reading dn / db, and the reduction overlaps whatever runs meanwhile.
+    Returns (dn, db), or the Work when async_op is True.
     """
     import torch.distributed as dist
     k = dn.numel()
+    flat = _adjacent_span(dn, db)
+    if flat is not None:
+        work = dist.all_reduce(flat, group=group, async_op=async_op)
+        return work if async_op else (dn, db)
+    if async_op:
+        raise ValueError("async_op needs dn and db adjacent in one buffer (as the SSA backward "
+                         "returns them)")
     buf = buffer if buffer is not None else torch.empty(k + 1, dtype=torch.float32, device=dn.device)
     buf[:k].copy_(dn.reshape(-1))
     buf[k:k + 1].copy_(db.reshape(1))
@@ -53,3 +64,15 @@ def allreduce_ssa_param_grads(dn: torch.Tensor, db: torch.Tensor, group=None,
     dn.copy_(buf[:k].reshape(dn.shape))
     db.copy_(buf[k].reshape(db.shape))
     return dn, db
+
+
+def _adjacent_span(dn: torch.Tensor, db: torch.Tensor) -> Optional[torch.Tensor]:
+    """A 1-D view covering dn followed immediately by db, when they are laid out that way in one
+    storage (dn contiguous, same dtype and device); else None."""
+    k = dn.numel()
+    if (db.numel() != 1 or dn.dtype != db.dtype or dn.device != db.device
+            or not dn.is_contiguous()
+            or dn.untyped_storage().data_ptr() != db.untyped_storage().data_ptr()
+            or db.data_ptr() != dn.data_ptr() + k * dn.element_size()):
+        return None
+    return dn.reshape(-1).as_strided((k + 1,), (1,))

@@ -122,6 +122,14 @@ def ssa_flash_attn_forward(q, k, v, softmax_scale, ssa_n, ssa_b, causal=True):
     return out, m
 
 
+def _param_grad_pair(n, device):
+    """dn (n's shape) and db (0-d), fp32, as adjacent views of one buffer: a data-parallel
+    caller sums both across ranks with one in-place all-reduce and no copies."""
+    k = n.numel()
+    buf = torch.empty(k + 1, device=device, dtype=torch.float32)
+    return buf[:k].view(n.shape), buf[k]
+
+
 def ssa_flash_attn_backward(q, k, v, out, dout, m, softmax_scale, ssa_n, ssa_b, causal=True):
     """Backward (reference ssa_triton_kernel.py:795-897).
 
@@ -137,8 +145,7 @@ def ssa_flash_attn_backward(q, k, v, out, dout, m, softmax_scale, ssa_n, ssa_b, 
     q, k, v, dout = _prep(q, fam), _prep(k, fam), _prep(v, fam), _prep(dout, fam)
     out = out if out.stride(-1) == 1 else out.contiguous()
     dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
-    dn = torch.empty(n.shape, device=q.device, dtype=torch.float32)
-    db = torch.empty((), device=q.device, dtype=torch.float32)
+    dn, db = _param_grad_pair(n, q.device)
     ws_bytes = lib.ssa_attn_bwd_workspace_size(ctypes.byref(prob))
     ws = torch.empty(max(ws_bytes, 1), device=q.device, dtype=torch.uint8)
     with torch.cuda.device(q.device):
@@ -231,8 +238,7 @@ def ssa_flash_attn_varlen_backward(q, k, v, out, dout, lse, cu_seqlens, max_seql
     dq = alloc(q.shape, dtype=q.dtype, device=q.device)
     dk = alloc(k.shape, dtype=k.dtype, device=k.device)
     dv = alloc(v.shape, dtype=v.dtype, device=v.device)
-    dn = torch.empty(n.shape, device=q.device, dtype=torch.float32)
-    db = torch.empty((), device=q.device, dtype=torch.float32)
+    dn, db = _param_grad_pair(n, q.device)
     ws_bytes = lib.ssa_attn_bwd_workspace_size(ctypes.byref(prob))
     ws = torch.empty(max(ws_bytes, 1), device=q.device, dtype=torch.uint8)
     with torch.cuda.device(q.device):

@@ -55,6 +55,11 @@ def _worker(rank, world, port, q, k, v, do, n, b, out_q):
                             compute_dtype=torch.float64)
     dn, db = r["dn"].clone(), r["db"].clone()
     allreduce_ssa_param_grads(dn, db, buffer=torch.empty(dn.numel() + 1, dtype=torch.float64))
+    # the layout the SSA backward returns (dn, db adjacent in one buffer): in place, async
+    pair = torch.cat([r["dn"].reshape(-1), r["db"].reshape(1)])
+    dn2, db2 = pair[:dn.numel()].view(dn.shape), pair[dn.numel()]
+    allreduce_ssa_param_grads(dn2, db2, async_op=True).wait()
+    assert torch.equal(dn2, dn) and torch.equal(db2, db)
     out_q.put((rank, dn, db))
     dist.barrier()
     dist.destroy_process_group()
@@ -85,6 +90,20 @@ def test_sharded_dn_db_allreduce_matches_full_batch():
     for rank, dn, db in results:
         assert torch.allclose(dn, full["dn"], rtol=1e-12, atol=1e-12), rank
         assert torch.allclose(db, full["db"], rtol=1e-12, atol=1e-12), rank
+
+
+def test_adjacent_param_grads_reduce_in_place():
+    from SSA.shard import _adjacent_span, allreduce_ssa_param_grads
+    buf = torch.arange(5, dtype=torch.float32)
+    dn, db = buf[:4].view(4), buf[4]
+    span = _adjacent_span(dn, db)
+    assert span is not None and span.data_ptr() == buf.data_ptr() and span.numel() == 5
+    assert _adjacent_span(buf[:1].view(()), buf[1]) is not None  # scalar n
+    assert _adjacent_span(torch.zeros(4), torch.zeros(())) is None  # separate storages
+    assert _adjacent_span(buf[:3], buf[4]) is None  # gap
+    assert _adjacent_span(buf[:4].double(), buf[4]) is None  # dtype
+    with pytest.raises(ValueError, match="adjacent"):
+        allreduce_ssa_param_grads(torch.zeros(4), torch.zeros(()), async_op=True)
 
 
 def _failing_worker(rank, world, port, out_q):

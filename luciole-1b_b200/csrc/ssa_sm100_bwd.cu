@@ -76,9 +76,9 @@ struct BwdCfg {
   //   warps 0..3 / 4..7  P/dS for query halves 0 / 1   (regs raised to REGS_PDS)
   //   warps 8..11        dQ drain                       (REGS_DQ)
   //   warp 12 TMA producer, warp 13 MMA issuer, 14..15 idle (REGS_CTRL)
-  // Budget at launch: 512 threads x 128 = 65536; after the moves 2*128*176 + 128*88 + 128*72
-  // = 65536.
-  static constexpr uint32_t REGS_PDS = 176, REGS_DQ = 88, REGS_CTRL = 72;
+  // Budget at launch: 512 threads x 128 = 65536; after the moves 2*128*176 + 128*96 + 128*64
+  // = 65536 (no role spills at this split; the drain needs 96 for its two 32-column loads).
+  static constexpr uint32_t REGS_PDS = 176, REGS_DQ = 96, REGS_CTRL = 64;
   static constexpr int WARP_PRODUCER = 12, WARP_MMA = 13;
 };
 static_assert(BwdCfg::SMEM_BYTES <= 232448, "shared memory budget");

@@ -76,9 +76,9 @@ struct BwdCfg {
   //   warps 0..3 / 4..7  P/dS for query halves 0 / 1   (regs raised to REGS_PDS)
   //   warps 8..11        dQ drain                       (REGS_DQ)
   //   warp 12 TMA producer, warp 13 MMA issuer, 14..15 idle (REGS_CTRL)
-  // Budget at launch: 512 threads x 128 = 65536; after the moves 2*128*176 + 128*96 + 128*64
+  // Budget at launch: 512 threads x 128 = 65536; after the moves 2*128*168 + 128*96 + 128*80
   // = 65536 (no role spills at this split; the drain needs 96 for its two 32-column loads).
-  static constexpr uint32_t REGS_PDS = 176, REGS_DQ = 96, REGS_CTRL = 64;
+  static constexpr uint32_t REGS_PDS = 168, REGS_DQ = 96, REGS_CTRL = 80;
   static constexpr int WARP_PRODUCER = 12, WARP_MMA = 13;
 };
 static_assert(BwdCfg::SMEM_BYTES <= 232448, "shared memory budget");
@@ -414,12 +414,12 @@ __global__ void __launch_bounds__(512, 1)
       w = __all_sync(0xffffffffu, w);
       return w && !*abort_flag;
     };
-    uint32_t sx[32], dp[32];
+    uint32_t sx[16], dp[16];
     bool ok = wait_tile(0);
     if (ok) {  // chunk 0 of tile 0; later tiles' chunk 0 is fetched behind the previous stores
       tc_fence_after();
-      tmem_ld32(tS, sx);
-      tmem_ld32(tP, dp);
+      tmem_ld16(tS, sx);
+      tmem_ld16(tP, dp);
     }
     int st = 0, g = 0, tt = 0;  // ring stage, q-head within the group, tile within the head
     for (int t = 0; ok && t < T; ++t) {
@@ -438,53 +438,57 @@ __global__ void __launch_bounds__(512, 1)
       tmem_ld_wait_only();
       tmem_pin_n(sx);
       tmem_pin_n(dp);
-      // 2 chunks of 32 queries. Chunk 1's S / dP loads are issued after chunk 0 has been
-      // computed (so chunk 0 keeps every register for instruction-level parallelism) and are in
-      // flight while chunk 0's P^T and dS^T are stored; the next tile's chunk 0 is loaded while
-      // chunk 1's are stored.
+      // 4 chunks of 16 queries (16-wide chunks leave the compiler registers to overlap more
+      // element pairs than 32-wide ones). Chunk c + 1's S / dP loads are issued after chunk c
+      // has been computed and are in flight while chunk c's P^T and dS^T are stored; the next
+      // tile's chunk 0 is loaded while chunk 3's are stored.
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        uint32_t pk[16], dk[16];
+      for (int c = 0; c < 4; ++c) {
+        uint32_t pk[8], dk[8];
         // A chunk masked for every row of this warp (the lower part of a diagonal tile, or past
         // the sequence end) has P = dS = 0: its transform is skipped.
-        const bool dead = !full && ((p.causal && mh + c * 32 + 31 < n0 + quad * 32) ||
-                                    mh + c * 32 >= L || n0 + quad * 32 >= L);
+        const bool dead = !full && ((p.causal && mh + c * 16 + 15 < n0 + quad * 32) ||
+                                    mh + c * 16 >= L || n0 + quad * 32 >= L);
         if (dead) {
 #pragma unroll
-          for (int i = 0; i < 16; ++i) pk[i] = dk[i] = 0u;
+          for (int i = 0; i < 8; ++i) pk[i] = dk[i] = 0u;
         } else if (full)
-          bwd_chunk<32, BF16, false, true>(sx, dp, lrow + c * 32, drow + c * 32, n, cb, nbs,
-                                           mh + c * 32, qmin, L, j < L, dn_acc, db_acc, pk, dk);
+          bwd_chunk<16, BF16, false, true>(sx, dp, lrow + c * 16, drow + c * 16, n, cb, nbs,
+                                           mh + c * 16, qmin, L, j < L, dn_acc, db_acc, pk, dk);
         else
-          bwd_chunk<32, BF16, true, true>(sx, dp, lrow + c * 32, drow + c * 32, n, cb, nbs,
-                                          mh + c * 32, qmin, L, j < L, dn_acc, db_acc, pk, dk);
-        if (c == 0) {
-          tmem_ld32(tS + 32, sx);
-          tmem_ld32(tP + 32, dp);
-          // dV(t-1) must have read this half's P^T columns before they are rewritten.
-          bool okb = t == 0 || mbar_wait(bar(BB_BF), (t - 1) & 1, a.status);
-          if (!__all_sync(0xffffffffu, okb)) *abort_flag = 1;
-          tc_fence_after();
+          bwd_chunk<16, BF16, true, true>(sx, dp, lrow + c * 16, drow + c * 16, n, cb, nbs,
+                                          mh + c * 16, qmin, L, j < L, dn_acc, db_acc, pk, dk);
+        if (c < 3) {
+          tmem_ld16(tS + 16 * (c + 1), sx);
+          tmem_ld16(tP + 16 * (c + 1), dp);
+          if (c == 0) {
+            // dV(t-1) must have read this half's P^T columns before they are rewritten.
+            bool okb = t == 0 || mbar_wait(bar(BB_BF), (t - 1) & 1, a.status);
+            if (!__all_sync(0xffffffffu, okb)) *abort_flag = 1;
+            tc_fence_after();
+          }
         }
-        tmem_st16(tPT + c * 16, pk);
+        tmem_st8(tPT + c * 8, pk);
         // dS^T row r of this half's slab: 16-byte chunks, 128-byte swizzle (chunk ^ (row & 7))
 #pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
-          const int chunk = c * 4 + q4;
+        for (int q2 = 0; q2 < 2; ++q2) {
+          const int chunk = c * 2 + q2;
           *reinterpret_cast<uint4*>(dsrow + ((chunk ^ (r & 7)) << 4)) =
-              make_uint4(dk[q4 * 4], dk[q4 * 4 + 1], dk[q4 * 4 + 2], dk[q4 * 4 + 3]);
+              make_uint4(dk[q2 * 4], dk[q2 * 4 + 1], dk[q2 * 4 + 2], dk[q2 * 4 + 3]);
         }
-        if (c == 0) {
+        if (c < 3) {
           tmem_ld_wait_only();
           tmem_pin_n(sx);
           tmem_pin_n(dp);
-          tc_fence_before();
-          mbar_arrive(bar(BB_SC));  // this tile's S^T / dP^T columns may now be overwritten
+          if (c == 2) {
+            tc_fence_before();
+            mbar_arrive(bar(BB_SC));  // this tile's S^T / dP^T columns may now be overwritten
+          }
         } else if (t + 1 < T) {
           if (wait_tile(t + 1)) {
             tc_fence_after();
-            tmem_ld32(tS, sx);
-            tmem_ld32(tP, dp);
+            tmem_ld16(tS, sx);
+            tmem_ld16(tP, dp);
           } else {
             ok = false;
           }

@@ -1041,33 +1041,35 @@ __global__ void __launch_bounds__(512, 1)
       const float* drow = del_s + st * C::BT;
       uint8_t* dsrow = smem + C::OFF_DS + h * C::DS_BYTES + r * 128;
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        uint32_t pk[16], dk[16];
-        const uint32_t(&cs)[32] = c ? s1 : s0;
-        const uint32_t(&cd)[32] = c ? d1 : d0;
+      for (int c = 0; c < 4; ++c) {  // 16-query chunks: more element pairs overlap than at 32
+        uint32_t pk[8], dk[8];
+        const uint32_t(&cs)[16] =
+            *reinterpret_cast<const uint32_t(*)[16]>(&((c >> 1) ? s1 : s0)[16 * (c & 1)]);
+        const uint32_t(&cd)[16] =
+            *reinterpret_cast<const uint32_t(*)[16]>(&((c >> 1) ? d1 : d0)[16 * (c & 1)]);
         // A chunk masked for every row of this warp: P = dS = 0, transform skipped.
-        const bool dead = !full && ((p.causal && mh + c * 32 + 31 < n0 + quad * 32) ||
-                                    mh + c * 32 >= L || n0 + quad * 32 >= L);
+        const bool dead = !full && ((p.causal && mh + c * 16 + 15 < n0 + quad * 32) ||
+                                    mh + c * 16 >= L || n0 + quad * 32 >= L);
         if (dead) {
 #pragma unroll
-          for (int i = 0; i < 16; ++i) pk[i] = dk[i] = 0u;
+          for (int i = 0; i < 8; ++i) pk[i] = dk[i] = 0u;
         } else if (full)
-          bwd_chunk<32, BF16, false, false>(cs, cd, lrow + c * 32, drow + c * 32, n, cb, nbs, mh + c * 32,
-                                     qmin, L, j < L, dn_acc, db_acc, pk, dk);
+          bwd_chunk<16, BF16, false, false>(cs, cd, lrow + c * 16, drow + c * 16, n, cb, nbs,
+                                            mh + c * 16, qmin, L, j < L, dn_acc, db_acc, pk, dk);
         else
-          bwd_chunk<32, BF16, true, false>(cs, cd, lrow + c * 32, drow + c * 32, n, cb, nbs, mh + c * 32,
-                                    qmin, L, j < L, dn_acc, db_acc, pk, dk);
+          bwd_chunk<16, BF16, true, false>(cs, cd, lrow + c * 16, drow + c * 16, n, cb, nbs,
+                                           mh + c * 16, qmin, L, j < L, dn_acc, db_acc, pk, dk);
         if (c == 0) {  // dV of this group's previous tile must have read its P^T columns
           bool okb = t < 2 || mbar_wait(bar(B2_BF + h), ((t >> 1) - 1) & 1, a.status);
           if (!__all_sync(0xffffffffu, okb)) *abort_flag = 1;
           tc_fence_after();
         }
-        tmem_st16(tPT + c * 16, pk);
+        tmem_st8(tPT + c * 8, pk);
 #pragma unroll
-        for (int q4 = 0; q4 < 4; ++q4) {
-          const int chunk = c * 4 + q4;
+        for (int q2 = 0; q2 < 2; ++q2) {
+          const int chunk = c * 2 + q2;
           *reinterpret_cast<uint4*>(dsrow + ((chunk ^ (r & 7)) << 4)) =
-              make_uint4(dk[q4 * 4], dk[q4 * 4 + 1], dk[q4 * 4 + 2], dk[q4 * 4 + 3]);
+              make_uint4(dk[q2 * 4], dk[q2 * 4 + 1], dk[q2 * 4 + 2], dk[q2 * 4 + 3]);
         }
       }
       tmem_st_wait();

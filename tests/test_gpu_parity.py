@@ -113,6 +113,10 @@ CASES = [
     (1, 8, 2, 256, 64, True, torch.float16, True),
     (1, 4, 4, 130, 128, True, torch.float16, False),
     (1, 4, 2, 64, 64, True, torch.bfloat16, False),     # shorter than one tile
+    (1, 6, 2, 256, 64, True, torch.bfloat16, True),     # GQA ratio 3 (not a power of two)
+    (2, 4, 2, 144, 64, True, torch.bfloat16, False),    # one tile + 16: a lone 16-query chunk
+    (1, 4, 1, 47, 64, True, torch.bfloat16, True),      # ragged inside the first 16-query chunk
+    (1, 6, 3, 144, 128, True, torch.bfloat16, True),    # D = 128, GQA 2, ragged
 ]
 
 
@@ -408,6 +412,29 @@ def test_config2_full_size_slice(cuda_device):
     assert_lowp_close("dv", r["dv"][zb:zb + 1, g0:g0 + 1], ref["dv"])
     for t in r.values():
         assert torch.isfinite(t).all()
+
+
+def test_d128_long_sequence_slice(cuda_device):
+    """D = 128 at S = 4096 (the config-4 head dim, 32 key blocks per sequence), one kv group's
+    two q-heads checked against the fp64 oracle over the whole sequence."""
+    B, Hq, Hkv, N, D = 1, 4, 2, 4096, 128
+    gen = torch.Generator(device="cpu").manual_seed(7)
+    q = (torch.randn(B, Hq, N, D, generator=gen) * 0.5).to(torch.bfloat16)
+    k = (torch.randn(B, Hkv, N, D, generator=gen) * 0.5).to(torch.bfloat16)
+    v = (torch.randn(B, Hkv, N, D, generator=gen) * 0.5).to(torch.bfloat16)
+    do = torch.randn(B, Hq, N, D, generator=gen).to(torch.bfloat16)
+    n = 0.3 + 0.3 * torch.rand(Hq, generator=gen)
+    b = torch.tensor(0.8)
+    dev = cuda_device
+    r = run_fwd_bwd(q.to(dev), k.to(dev), v.to(dev), do.to(dev), D ** -0.5, n.to(dev), b.to(dev), True)
+    g0 = 1  # kv head 1 -> q heads 2, 3
+    hs = slice(2 * g0, 2 * g0 + 2)
+    ref = ssa_reference_grads(q[:, hs], k[:, g0:g0 + 1], v[:, g0:g0 + 1], D ** -0.5, n[hs], b,
+                              do[:, hs], True)
+    assert_lowp_close("out", r["out"][:, hs], ref["out"])
+    assert_lowp_close("dq", r["dq"][:, hs], ref["dq"])
+    assert_lowp_close("dk", r["dk"][:, g0:g0 + 1], ref["dk"])
+    assert_lowp_close("dv", r["dv"][:, g0:g0 + 1], ref["dv"])
 
 
 def test_device_timeout_path_reports_and_recovers(cuda_device):

@@ -350,28 +350,31 @@ __global__ void __launch_bounds__(kNT) bwd_dq_generic_kernel(Problem p, TensorRe
 // dn / db: deterministic fp64 reduction of per-tile partials laid out [Z][Hq][P]. Block h < nh
 // sums dn for head h (or, for a scalar n, every partial); block nh sums db. Each thread walks a
 // fixed strided subset, then a fixed tree: the result does not depend on scheduling.
-__global__ void __launch_bounds__(kNT) dndb_reduce_kernel(const float* dn_part,
-                                                          const float* db_part, int Z, int Hq,
-                                                          int P, int n_per_head, float* dn,
-                                                          float* db) {
-  __shared__ double red[kNT];
+// 1024 threads per block: the db block sums every partial of the call (B * Hq * P values), so its
+// per-thread loop is what bounds this kernel's time.
+constexpr int kRedNT = 1024;
+__global__ void __launch_bounds__(kRedNT) dndb_reduce_kernel(const float* dn_part,
+                                                             const float* db_part, int Z, int Hq,
+                                                             int P, int n_per_head, float* dn,
+                                                             float* db) {
+  __shared__ double red[kRedNT];
   const int tid = threadIdx.x;
   const int nh = n_per_head ? Hq : 1;
   const int h = blockIdx.x;
   const int64_t per_head = (int64_t)Z * P;
   double s = 0.0;
   if (h < nh && n_per_head) {
-    for (int64_t i = tid; i < per_head; i += kNT) {
+    for (int64_t i = tid; i < per_head; i += kRedNT) {
       const int64_t zz = i / P, pp = i - zz * P;
       s += (double)dn_part[(zz * Hq + h) * P + pp];
     }
   } else {
     const float* src = h < nh ? dn_part : db_part;
-    for (int64_t i = tid; i < per_head * Hq; i += kNT) s += (double)src[i];
+    for (int64_t i = tid; i < per_head * Hq; i += kRedNT) s += (double)src[i];
   }
   red[tid] = s;
   __syncthreads();
-  for (int o = kNT / 2; o > 0; o >>= 1) {
+  for (int o = kRedNT / 2; o > 0; o >>= 1) {
     if (tid < o) red[tid] += red[tid + o];
     __syncthreads();
   }
@@ -486,7 +489,7 @@ int launch_bwd_generic(int dtype, const Problem& p, TensorRef q, TensorRef k, Te
 int launch_dndb_reduce(const float* dn_part, const float* db_part, int Z, int Hq, int P,
                        int n_per_head, float* dn, float* db, cudaStream_t st) {
   const int blocks = (n_per_head ? Hq : 1) + 1;
-  dndb_reduce_kernel<<<blocks, kNT, 0, st>>>(dn_part, db_part, Z, Hq, P, n_per_head, dn, db);
+  dndb_reduce_kernel<<<blocks, kRedNT, 0, st>>>(dn_part, db_part, Z, Hq, P, n_per_head, dn, db);
   note_launches(1);
   return SSA_OK;
 }

@@ -96,4 +96,38 @@ __device__ __forceinline__ float ssa_signed_log1p(float s, float b, float& inv_1
   return s > 0.f ? l : (s < 0.f ? -l : 0.f);
 }
 
+
+// dn / db: deterministic fp64 reduction of per-tile partials laid out [Z][Hq][P], by one block of
+// NT threads. Block h < nh (nh = Hq for a per-head n, else 1) sums dn for head h (or, for a
+// scalar n, every partial); block nh sums db. Each thread walks a fixed strided subset, then a
+// fixed tree: the result does not depend on scheduling. red: NT doubles of shared memory.
+template <int NT>
+__device__ __forceinline__ void dndb_reduce_block(int h, const float* dn_part, const float* db_part,
+                                                  int Z, int Hq, int P, int n_per_head, float* dn,
+                                                  float* db, double* red) {
+  const int tid = threadIdx.x;
+  const int nh = n_per_head ? Hq : 1;
+  const int64_t per_head = (int64_t)Z * P;
+  double s = 0.0;
+  if (h < nh && n_per_head) {
+    for (int64_t i = tid; i < per_head; i += NT) {
+      const int64_t zz = i / P, pp = i - zz * P;
+      s += (double)dn_part[(zz * Hq + h) * P + pp];
+    }
+  } else {
+    const float* src = h < nh ? dn_part : db_part;
+    for (int64_t i = tid; i < per_head * Hq; i += NT) s += (double)src[i];
+  }
+  red[tid] = s;
+  __syncthreads();
+  for (int o = NT / 2; o > 0; o >>= 1) {
+    if (tid < o) red[tid] += red[tid + o];
+    __syncthreads();
+  }
+  if (tid == 0) {
+    if (h < nh) dn[h] = (float)red[0];
+    else db[0] = (float)red[0];
+  }
+}
+
 }  // namespace ssa

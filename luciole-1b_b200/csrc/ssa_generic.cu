@@ -347,41 +347,16 @@ __global__ void __launch_bounds__(kNT) bwd_dq_generic_kernel(Problem p, TensorRe
 }
 
 // ---------------------------------------------------------------------------------------------
-// dn / db: deterministic fp64 reduction of per-tile partials laid out [Z][Hq][P]. Block h < nh
-// sums dn for head h (or, for a scalar n, every partial); block nh sums db. Each thread walks a
-// fixed strided subset, then a fixed tree: the result does not depend on scheduling.
-// 1024 threads per block: the db block sums every partial of the call (B * Hq * P values), so its
-// per-thread loop is what bounds this kernel's time.
+// dn / db reduction as its own launch (generic path and the allocation-free backward): one block
+// per dn head plus one for db (dndb_reduce_block). 1024 threads per block: the db block sums every
+// partial of the call (B * Hq * P values), so its per-thread loop bounds this kernel's time.
 constexpr int kRedNT = 1024;
 __global__ void __launch_bounds__(kRedNT) dndb_reduce_kernel(const float* dn_part,
                                                              const float* db_part, int Z, int Hq,
                                                              int P, int n_per_head, float* dn,
                                                              float* db) {
   __shared__ double red[kRedNT];
-  const int tid = threadIdx.x;
-  const int nh = n_per_head ? Hq : 1;
-  const int h = blockIdx.x;
-  const int64_t per_head = (int64_t)Z * P;
-  double s = 0.0;
-  if (h < nh && n_per_head) {
-    for (int64_t i = tid; i < per_head; i += kRedNT) {
-      const int64_t zz = i / P, pp = i - zz * P;
-      s += (double)dn_part[(zz * Hq + h) * P + pp];
-    }
-  } else {
-    const float* src = h < nh ? dn_part : db_part;
-    for (int64_t i = tid; i < per_head * Hq; i += kRedNT) s += (double)src[i];
-  }
-  red[tid] = s;
-  __syncthreads();
-  for (int o = kRedNT / 2; o > 0; o >>= 1) {
-    if (tid < o) red[tid] += red[tid + o];
-    __syncthreads();
-  }
-  if (tid == 0) {
-    if (h < nh) dn[h] = (float)red[0];
-    else db[0] = (float)red[0];
-  }
+  dndb_reduce_block<kRedNT>(blockIdx.x, dn_part, db_part, Z, Hq, P, n_per_head, dn, db, red);
 }
 
 template <typename T, int D>

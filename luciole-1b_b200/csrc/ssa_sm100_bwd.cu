@@ -661,12 +661,35 @@ __global__ void __launch_bounds__(256) bwd_preprocess_sm100_kernel(Problem p, Te
   }
 }
 
-// dq (q's dtype, caller strides) = dq_accum (fp32) for the valid rows.
+// dq (q's dtype, caller strides) = dq_accum (fp32) for the valid rows. The first grid rows
+// (r.rows of them) reduce dn / db instead (dndb_reduce_block, one block per dn head plus one for
+// db): dispatched first, that latency-bound work runs under the bandwidth-bound conversion
+// rather than as a launch of its own or as a tail after it.
+struct DndbArgs {
+  const float* dn_part;
+  const float* db_part;
+  int P;     // partials per (sequence, q-head)
+  int rows;  // leading grid rows that reduce
+  float* dn;
+  float* db;
+};
+
 template <typename T, int D>
 __global__ void __launch_bounds__(256) dq_convert_kernel(Problem p, const float* dq_accum,
-                                                         int64_t dq_rows, TensorRef dq) {
+                                                         int64_t dq_rows, TensorRef dq,
+                                                         DndbArgs r) {
+  if ((int)blockIdx.y < r.rows) {
+    __shared__ double red[256];
+    const int nred = (p.n_per_head ? p.Hq : 1) + 1;
+    const int h = (int)blockIdx.y * (int)gridDim.x + (int)blockIdx.x;
+    if (h < nred)  // uniform per block
+      dndb_reduce_block<256>(h, r.dn_part, r.db_part, p.B, p.Hq, r.P, p.n_per_head, r.dn, r.db,
+                             red);
+    return;
+  }
   constexpr int TPR = D / 8, RPB = 256 / TPR;
-  const int z = blockIdx.y / p.Hq, hq = blockIdx.y % p.Hq;
+  const int zh = (int)blockIdx.y - r.rows;
+  const int z = zh / p.Hq, hq = zh % p.Hq;
   int seq_start, L;
   seq_bounds(p, z, seq_start, L);
   const int row = blockIdx.x * RPB + threadIdx.x / TPR;
@@ -686,6 +709,21 @@ __global__ void __launch_bounds__(256) dq_convert_kernel(Problem p, const float*
                    pack2<false>(a1.z, a1.w));
   }
   *reinterpret_cast<uint4*>(d) = w;
+}
+
+// dq conversion + dn / db reduction, one launch.
+template <typename T, int D>
+void launch_dq_convert_dndb(const Problem& p, const float* dq_accum, int64_t dq_rows,
+                            TensorRef dq, const float* dn_part, const float* db_part, int P,
+                            float* dn, float* db, cudaStream_t st) {
+  constexpr int RPB = 256 / (D / 8);
+  const int gx = (p.max_seqlen + RPB - 1) / RPB;
+  const int nred = (p.n_per_head ? p.Hq : 1) + 1;
+  const int extra_rows = (nred + gx - 1) / gx;
+  dim3 gc((unsigned)gx, (unsigned)(p.B * p.Hq + extra_rows));
+  dq_convert_kernel<T, D><<<gc, 256, 0, st>>>(p, dq_accum, dq_rows, dq,
+                                              DndbArgs{dn_part, db_part, P, extra_rows, dn, db});
+  note_launches(1);
 }
 
 // ============================================================================================
@@ -1259,12 +1297,11 @@ int run_bwd(const Problem& p, TensorRef q, TensorRef k, TensorRef v, TensorRef o
     return SSA_ERR_CUDA;
   const long long grid = (long long)lay.nkv * p.B * p.Hkv;
   kern<<<(unsigned)grid, C::THREADS, C::SMEM_BYTES, st>>>(tq, tk, tv, tdo, tdq, a);
+  note_launches(1);
   using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
-  dim3 gc((p.max_seqlen + 31) / 32, p.B * p.Hq);
-  dq_convert_kernel<T, 64><<<gc, 256, 0, st>>>(p, a.dq_accum, a.dq_rows, dq);
-  note_launches(2);
-  return launch_dndb_reduce(a.dn_part, a.db_part, p.B, p.Hq, 8 * lay.nkv, p.n_per_head, dn, db,
-                            st);
+  launch_dq_convert_dndb<T, 64>(p, a.dq_accum, a.dq_rows, dq, a.dn_part, a.db_part, 8 * lay.nkv,
+                                dn, db, st);
+  return SSA_OK;
 }
 
 template <bool BF16>
@@ -1318,11 +1355,10 @@ int run_bwd128(const Problem& p, TensorRef q, TensorRef k, TensorRef v, TensorRe
     return SSA_ERR_CUDA;
   const long long grid = (long long)lay.nkv * p.B * p.Hkv;
   kern<<<(unsigned)grid, C::THREADS, C::SMEM_BYTES, st>>>(tq, tk, tv, tdo, tdq, a);
-  dim3 gc((p.max_seqlen + 15) / 16, p.B * p.Hq);
-  dq_convert_kernel<T, 128><<<gc, 256, 0, st>>>(p, a.dq_accum, a.dq_rows, dq);
-  note_launches(3);
-  return launch_dndb_reduce(a.dn_part, a.db_part, p.B, p.Hq, 8 * lay.nkv, p.n_per_head, dn, db,
-                            st);
+  note_launches(2);
+  launch_dq_convert_dndb<T, 128>(p, a.dq_accum, a.dq_rows, dq, a.dn_part, a.db_part, 8 * lay.nkv,
+                                 dn, db, st);
+  return SSA_OK;
 }
 
 }  // namespace sm100

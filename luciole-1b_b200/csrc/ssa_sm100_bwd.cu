@@ -259,6 +259,9 @@ __global__ void __launch_bounds__(512, 1)
         }
       }
     };
+    // delta comes from the preprocess kernel, which may still be running (programmatic launch):
+    // K / V above and the first Q / dO tiles below do not depend on it.
+    griddep_wait();
     fetch_stats(0);
     for (int t = 0; t < T; ++t) {
       const int st = t % C::STAGES, u = t / C::STAGES;
@@ -557,6 +560,7 @@ __global__ void __launch_bounds__(512, 1)
     // The drain's arrival for tile t's barrier SM(t) says dQ(t-1) has left TMEM; tile 0 has no
     // predecessor.
     mbar_arrive(bar(BB_SM));
+    griddep_wait();  // the dQ accumulator is zeroed by the preprocess kernel
     bool ok = true;
     for (int t = 0; t < T; ++t) {
       ok = mbar_wait(bar(BB_DQF), t & 1, a.status);
@@ -620,6 +624,7 @@ __global__ void __launch_bounds__(256) bwd_preprocess_sm100_kernel(Problem p, Te
                                                                    TensorRef dout, float* delta,
                                                                    float* dq_accum,
                                                                    int64_t dq_rows) {
+  griddep_launch_dependents();  // the backward's setup may overlap this pass
   constexpr int TPR = D / 8, RPB = 256 / TPR;
   const int sub = threadIdx.x % TPR;
   const int rr = blockIdx.x * RPB + threadIdx.x / TPR;  // row within the head's accumulator
@@ -678,6 +683,7 @@ template <typename T, int D>
 __global__ void __launch_bounds__(256) dq_convert_kernel(Problem p, const float* dq_accum,
                                                          int64_t dq_rows, TensorRef dq,
                                                          DndbArgs r) {
+  griddep_wait();  // launched programmatically behind the backward kernel
   if ((int)blockIdx.y < r.rows) {
     __shared__ double red[256];
     const int nred = (p.n_per_head ? p.Hq : 1) + 1;
@@ -711,6 +717,24 @@ __global__ void __launch_bounds__(256) dq_convert_kernel(Problem p, const float*
   *reinterpret_cast<uint4*>(d) = w;
 }
 
+// Launch with programmatic stream serialization (the kernel may start before the previous one on
+// the stream has finished; it calls griddep_wait() before touching that kernel's results).
+template <typename... KArgs, typename... Args>
+void launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
 // dq conversion + dn / db reduction, one launch.
 template <typename T, int D>
 void launch_dq_convert_dndb(const Problem& p, const float* dq_accum, int64_t dq_rows,
@@ -721,8 +745,8 @@ void launch_dq_convert_dndb(const Problem& p, const float* dq_accum, int64_t dq_
   const int nred = (p.n_per_head ? p.Hq : 1) + 1;
   const int extra_rows = (nred + gx - 1) / gx;
   dim3 gc((unsigned)gx, (unsigned)(p.B * p.Hq + extra_rows));
-  dq_convert_kernel<T, D><<<gc, 256, 0, st>>>(p, dq_accum, dq_rows, dq,
-                                              DndbArgs{dn_part, db_part, P, extra_rows, dn, db});
+  launch_pdl(dq_convert_kernel<T, D>, gc, dim3(256), 0, st, p, dq_accum, dq_rows, dq,
+             DndbArgs{dn_part, db_part, P, extra_rows, dn, db});
   note_launches(1);
 }
 
@@ -1296,7 +1320,8 @@ int run_bwd(const Problem& p, TensorRef q, TensorRef k, TensorRef v, TensorRef o
   if (set_smem_limit_once(reinterpret_cast<const void*>(kern), (int)C::SMEM_BYTES) != SSA_OK)
     return SSA_ERR_CUDA;
   const long long grid = (long long)lay.nkv * p.B * p.Hkv;
-  kern<<<(unsigned)grid, C::THREADS, C::SMEM_BYTES, st>>>(tq, tk, tv, tdo, tdq, a);
+  launch_pdl(kern, dim3((unsigned)grid), dim3(C::THREADS), C::SMEM_BYTES, st, tq, tk, tv, tdo, tdq,
+             a);
   note_launches(1);
   using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
   launch_dq_convert_dndb<T, 64>(p, a.dq_accum, a.dq_rows, dq, a.dn_part, a.db_part, 8 * lay.nkv,

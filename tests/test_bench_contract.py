@@ -1,0 +1,51 @@
+"""bench.py on the CPU: the FLOP accounting of each workload (the FlashAttention convention,
+14 * D per causal score element) and the reference arm's JSON line, which runs the CPU oracle
+and needs no GPU."""
+
+import json
+import subprocess
+import sys
+from pathlib import Path
+
+import pytest
+
+REPO = Path(__file__).resolve().parent.parent
+
+
+@pytest.fixture
+def bench():
+    sys.path.insert(0, str(REPO))
+    import bench as b
+    yield b
+    b.select_config("c2")
+
+
+def test_flop_counts_match_the_workloads(bench):
+    bench.select_config("c2")  # B=8, Hq=32, S=2048, D=64, causal: E = 8*32*2048^2/2
+    assert bench.score_elements() == 8 * 32 * 2048 * 2048 // 2 == 536870912
+    assert bench.flops_per_rank() == pytest.approx(4.810e11, rel=1e-3)
+    assert bench.flops_bwd_per_rank() == pytest.approx(10 * 64 * 536870912)
+    bench.select_config("c4")  # B=1, Hq=32, S=32768, D=128
+    assert bench.flops_per_rank() == pytest.approx(3.079e13, rel=1e-3)
+    bench.select_config("c3")  # packed documents: E = Hq * sum(L^2 / 2)
+    lens = bench.DOC_LENS
+    assert sum(lens) == 65536 and all(1 <= L <= 4096 for L in lens)
+    assert bench.score_elements() == 32 * sum(L * L // 2 for L in lens)
+
+
+def test_reference_arm_prints_one_contract_line():
+    r = subprocess.run([sys.executable, "bench.py", "--impl", "reference", "--steps", "3",
+                        "--warmup", "3"], cwd=REPO, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stderr[-2000:]
+    lines = [l for l in r.stdout.splitlines() if l.startswith("{")]
+    assert len(lines) == 1
+    d = json.loads(lines[0])
+    assert d["impl"] == "reference"
+    for key in ("metric", "value", "unit", "n_gpus", "steps", "warmup", "higher_is_better",
+                "scaling", "vs_baseline", "dtype", "data", "config", "cpu_baseline", "e2e"):
+        assert key in d, key
+    assert d["unit"] == "TFLOP/s" and d["higher_is_better"] is True and d["value"] > 0
+    assert d["steps"] == 3 and d["warmup"] >= 3 and d["n_gpus"] == 1
+    assert d["cpu_baseline"]["kind"] in ("port", "reference") and d["cpu_baseline"]["cores"] >= 1
+    assert d["e2e"]["value"] == d["value"]
+    assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["e2e"]["d2h_bytes_per_step"] == 0

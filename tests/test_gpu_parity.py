@@ -414,6 +414,31 @@ def test_config2_full_size_slice(cuda_device):
         assert torch.isfinite(t).all()
 
 
+@pytest.mark.parametrize("D", [64, 128])
+def test_negative_and_large_n_large_scores(D, cuda_device):
+    """Per-head n of both signs and up to 2.5 with scores of larger magnitude (q, k scaled 1.5):
+    the forward's normaliser bound (|n| log2(1 + b max|s|)) and its rescaling both come into
+    play, and for n < 0 the largest transformed score comes from the most negative s."""
+    K = _api()
+    B, Hq, Hkv, N = 1, 4, 2, 384
+    seed = 900 + D
+    q = seeded((B, Hq, N, D), seed, 1.5)
+    k = seeded((B, Hkv, N, D), seed + 1, 1.5)
+    v = seeded((B, Hkv, N, D), seed + 2, 0.5)
+    do = seeded((B, Hq, N, D), seed + 3, 1.0)
+    n = torch.tensor([-1.5, -0.4, 0.9, 2.5])
+    b = torch.tensor(0.8)
+    scale = 1.0 / math.sqrt(D)
+    assert K.kernel_family(q.to(cuda_device), scale) == 1
+    r = run_fwd_bwd(q.to(cuda_device), k.to(cuda_device), v.to(cuda_device), do.to(cuda_device),
+                    scale, n.to(cuda_device), b.to(cuda_device), True)
+    ref = ssa_reference_grads(q, k, v, scale, n, b, do, True)
+    for name in ("out", "dq", "dk", "dv"):
+        assert_lowp_close(name, r[name], ref[name])
+    assert_scalar_close("dn", r["dn"], ref["dn"])
+    assert_scalar_close("db", r["db"], ref["db"])
+
+
 def test_d128_long_sequence_slice(cuda_device):
     """D = 128 at S = 4096 (the config-4 head dim, 32 key blocks per sequence), one kv group's
     two q-heads checked against the fp64 oracle over the whole sequence."""

@@ -720,8 +720,8 @@ __global__ void __launch_bounds__(256) dq_convert_kernel(Problem p, const float*
 // Launch with programmatic stream serialization (the kernel may start before the previous one on
 // the stream has finished; it calls griddep_wait() before touching that kernel's results).
 template <typename... KArgs, typename... Args>
-void launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
-                Args&&... args) {
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                       Args&&... args) {
   cudaLaunchConfig_t cfg = {};
   cfg.gridDim = grid;
   cfg.blockDim = block;
@@ -732,12 +732,12 @@ void launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cuda
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
 // dq conversion + dn / db reduction, one launch.
 template <typename T, int D>
-void launch_dq_convert_dndb(const Problem& p, const float* dq_accum, int64_t dq_rows,
+int launch_dq_convert_dndb(const Problem& p, const float* dq_accum, int64_t dq_rows,
                             TensorRef dq, const float* dn_part, const float* db_part, int P,
                             float* dn, float* db, cudaStream_t st) {
   constexpr int RPB = 256 / (D / 8);
@@ -745,9 +745,11 @@ void launch_dq_convert_dndb(const Problem& p, const float* dq_accum, int64_t dq_
   const int nred = (p.n_per_head ? p.Hq : 1) + 1;
   const int extra_rows = (nred + gx - 1) / gx;
   dim3 gc((unsigned)gx, (unsigned)(p.B * p.Hq + extra_rows));
-  launch_pdl(dq_convert_kernel<T, D>, gc, dim3(256), 0, st, p, dq_accum, dq_rows, dq,
-             DndbArgs{dn_part, db_part, P, extra_rows, dn, db});
+  if (launch_pdl(dq_convert_kernel<T, D>, gc, dim3(256), 0, st, p, dq_accum, dq_rows, dq,
+                 DndbArgs{dn_part, db_part, P, extra_rows, dn, db}) != cudaSuccess)
+    return SSA_ERR_LAUNCH;
   note_launches(1);
+  return SSA_OK;
 }
 
 // ============================================================================================
@@ -1320,13 +1322,13 @@ int run_bwd(const Problem& p, TensorRef q, TensorRef k, TensorRef v, TensorRef o
   if (set_smem_limit_once(reinterpret_cast<const void*>(kern), (int)C::SMEM_BYTES) != SSA_OK)
     return SSA_ERR_CUDA;
   const long long grid = (long long)lay.nkv * p.B * p.Hkv;
-  launch_pdl(kern, dim3((unsigned)grid), dim3(C::THREADS), C::SMEM_BYTES, st, tq, tk, tv, tdo, tdq,
-             a);
+  if (launch_pdl(kern, dim3((unsigned)grid), dim3(C::THREADS), C::SMEM_BYTES, st, tq, tk, tv, tdo,
+                 tdq, a) != cudaSuccess)
+    return SSA_ERR_LAUNCH;
   note_launches(1);
   using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
-  launch_dq_convert_dndb<T, 64>(p, a.dq_accum, a.dq_rows, dq, a.dn_part, a.db_part, 8 * lay.nkv,
-                                dn, db, st);
-  return SSA_OK;
+  return launch_dq_convert_dndb<T, 64>(p, a.dq_accum, a.dq_rows, dq, a.dn_part, a.db_part,
+                                       8 * lay.nkv, dn, db, st);
 }
 
 template <bool BF16>
@@ -1381,9 +1383,8 @@ int run_bwd128(const Problem& p, TensorRef q, TensorRef k, TensorRef v, TensorRe
   const long long grid = (long long)lay.nkv * p.B * p.Hkv;
   kern<<<(unsigned)grid, C::THREADS, C::SMEM_BYTES, st>>>(tq, tk, tv, tdo, tdq, a);
   note_launches(2);
-  launch_dq_convert_dndb<T, 128>(p, a.dq_accum, a.dq_rows, dq, a.dn_part, a.db_part, 8 * lay.nkv,
-                                 dn, db, st);
-  return SSA_OK;
+  return launch_dq_convert_dndb<T, 128>(p, a.dq_accum, a.dq_rows, dq, a.dn_part, a.db_part,
+                                        8 * lay.nkv, dn, db, st);
 }
 
 }  // namespace sm100

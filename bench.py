@@ -103,6 +103,28 @@ def flops_bwd_per_rank() -> float:
     return 10.0 * D * score_elements()
 
 
+# The SSA transform's special-function work (not counted in the FLOPs): lg2 and ex2 per score
+# element in the forward and again in the backward (the reciprocal runs on the FMA pipe). B200
+# issues 16 such operations per clock per SM.
+SFU_OPS_PER_ELEMENT = 4
+SFU_OPS_PER_CLK_SM = 16
+
+
+def sfu_floor(ms_per_step: float) -> dict:
+    """The special-function floor of one step (algorithmic elements, max SM clock) and the
+    fraction of it the measured step reaches."""
+    sms = torch.cuda.get_device_properties(0).multi_processor_count if torch.cuda.is_available() else 148
+    mhz = 1965.0
+    p = REPO / "MEASURED_PEAKS.json"
+    if p.exists():
+        mhz = float(json.loads(p.read_text()).get("sm_max_mhz", mhz))
+    ops = SFU_OPS_PER_ELEMENT * score_elements()
+    peak = SFU_OPS_PER_CLK_SM * sms * mhz * 1e6
+    floor_ms = ops / peak * 1e3
+    return {"ops_per_step": ops, "peak_ops_per_s": peak, "floor_ms": floor_ms,
+            "frac": floor_ms / ms_per_step}
+
+
 def measured_peaks():
     p = REPO / "MEASURED_PEAKS.json"
     if p.exists():
@@ -595,7 +617,10 @@ def main():
             "roofline": {"bound": "tensor", "kernel": "ssa_attn_bwd call (dominant)",
                          "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
                          "frac": achieved / peak_tf, "peak_kind": f"{peak_kind} bf16 burst",
-                         "traffic": NCU_TRAFFIC_BYTES if args.config == "c2" else None},
+                         "traffic": NCU_TRAFFIC_BYTES if args.config == "c2" else None,
+                         # what bounds SSA at D = 64: the special-function unit (lg2 / ex2)
+                         # (context parallelism: each rank has 1/world of the job's elements)
+                         "sfu": sfu_floor(ms * (world if args.cp else 1))},
             "cpu_baseline": cpu,
             "clocks": clk.summary(),
             "gpu_launches": launches,

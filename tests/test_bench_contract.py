@@ -27,6 +27,11 @@ def test_flop_counts_match_the_workloads(bench):
     assert bench.flops_bwd_per_rank() == pytest.approx(10 * 64 * 536870912)
     bench.select_config("c4")  # B=1, Hq=32, S=32768, D=128
     assert bench.flops_per_rank() == pytest.approx(3.079e13, rel=1e-3)
+    # special-function floor: lg2 + ex2 per element in each direction at 16 per clock per SM
+    sf = bench.sfu_floor(1.0)
+    assert sf["ops_per_step"] == 4 * bench.score_elements()
+    assert sf["floor_ms"] == pytest.approx(sf["ops_per_step"] / sf["peak_ops_per_s"] * 1e3)
+    assert sf["frac"] == pytest.approx(sf["floor_ms"])
     bench.select_config("c3")  # packed documents: E = Hq * sum(L^2 / 2)
     lens = bench.DOC_LENS
     assert sum(lens) == 65536 and all(1 <= L <= 4096 for L in lens)

@@ -259,8 +259,8 @@ __global__ void __launch_bounds__(512, 1)
         }
       }
     };
-    // delta comes from the preprocess kernel, which may still be running (programmatic launch):
-    // K / V above and the first Q / dO tiles below do not depend on it.
+    // delta comes from the preprocess kernel, which may still be running (programmatic launch);
+    // the K / V loads above do not depend on it.
     griddep_wait();
     fetch_stats(0);
     for (int t = 0; t < T; ++t) {

@@ -419,7 +419,7 @@ __global__ void __launch_bounds__(512, 1)
     };
     uint32_t sx[16], dp[16];
     bool ok = wait_tile(0);
-    if (ok) {  // chunk 0 of tile 0; later tiles' chunk 0 is fetched behind the previous stores
+    if (ok) {  // chunk 0 of tile 0; later tiles' chunk 0 is fetched after the previous tile's SM
       tc_fence_after();
       tmem_ld16(tS, sx);
       tmem_ld16(tP, dp);
@@ -443,8 +443,9 @@ __global__ void __launch_bounds__(512, 1)
       tmem_pin_n(dp);
       // 4 chunks of 16 queries (16-wide chunks leave the compiler registers to overlap more
       // element pairs than 32-wide ones). Chunk c + 1's S / dP loads are issued after chunk c
-      // has been computed and are in flight while chunk c's P^T and dS^T are stored; the next
-      // tile's chunk 0 is loaded while chunk 3's are stored.
+      // has been computed and are in flight while chunk c's P^T and dS^T are stored. After
+      // chunk 3 the tile's SM arrival goes first (the grads MMAs wait on it), then the next
+      // tile's chunk 0 is loaded.
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         uint32_t pk[8], dk[8];
@@ -487,20 +488,21 @@ __global__ void __launch_bounds__(512, 1)
             tc_fence_before();
             mbar_arrive(bar(BB_SC));  // this tile's S^T / dP^T columns may now be overwritten
           }
-        } else if (t + 1 < T) {
-          if (wait_tile(t + 1)) {
-            tc_fence_after();
-            tmem_ld16(tS, sx);
-            tmem_ld16(tP, dp);
-          } else {
-            ok = false;
-          }
         }
       }
       tmem_st_wait();
       tc_fence_before();
       fence_proxy_async_smem();
       mbar_arrive(bar(BB_SM));
+      if (t + 1 < T) {
+        if (wait_tile(t + 1)) {
+          tc_fence_after();
+          tmem_ld16(tS, sx);
+          tmem_ld16(tP, dp);
+        } else {
+          ok = false;
+        }
+      }
       if (tt == T_h - 1) {  // end of q-head g: each warp writes its dn/db partial
         float x1 = (dn_acc[0].x + dn_acc[0].y) + (dn_acc[1].x + dn_acc[1].y);
         float x2 = (db_acc[0].x + db_acc[0].y) + (db_acc[1].x + db_acc[1].y);

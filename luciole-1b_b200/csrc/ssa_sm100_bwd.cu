@@ -124,31 +124,52 @@ __device__ __forceinline__ void bwd_chunk(const uint32_t (&sx)[W], const uint32_
                                           float2 (&dn_acc)[2], float2 (&db_acc)[2],
                                           uint32_t (&pk)[W / 2], uint32_t (&dk)[W / 2]) {
   const float2 n2 = make_float2(n, n), nbs2 = make_float2(nbs, nbs);
+  float slv[W], rv[W];
+  float2 prv[W / 2];
+  // Three passes over the chunk: sign * log2(1 + u) and 1/(1 + u) per element, then the
+  // exponentials, then the rest. The operations and results are those of one pass per element
+  // pair; the phased order measured 1.5% faster in the config-2 backward.
+#pragma unroll
+  for (int e = 0; e < W; e += 2) {
+    const float x0 = __uint_as_float(sx[e]), x1 = __uint_as_float(sx[e + 1]);
+    const float a0 = fmaf(fabsf(x0), cb, 1.0f), a1 = fmaf(fabsf(x1), cb, 1.0f);
+    slv[e] = copy_sign_bit(lg2_approx(a0), x0);
+    slv[e + 1] = copy_sign_bit(lg2_approx(a1), x1);
+    const float2 r =
+        NRCP ? rcp2_newton(make_float2(a0, a1)) : make_float2(rcp_approx(a0), rcp_approx(a1));
+    rv[e] = r.x;
+    rv[e + 1] = r.y;
+  }
 #pragma unroll
   for (int e4 = 0; e4 < W / 4; ++e4) {
     const float4 nl = *reinterpret_cast<const float4*>(lrow + e4 * 4);
+#pragma unroll
+    for (int pi = 0; pi < 2; ++pi) {
+      const int e = e4 * 4 + pi * 2;
+      const float2 nlse = pi ? make_float2(nl.z, nl.w) : make_float2(nl.x, nl.y);
+      const float2 t = __ffma2_rn(n2, make_float2(slv[e], slv[e + 1]), nlse);
+      prv[e / 2] = make_float2(ex2_approx(t.x), ex2_approx(t.y));
+    }
+  }
+#pragma unroll
+  for (int e4 = 0; e4 < W / 4; ++e4) {
     const float4 nd = *reinterpret_cast<const float4*>(drow + e4 * 4);
 #pragma unroll
     for (int pi = 0; pi < 2; ++pi) {
       const int e = e4 * 4 + pi * 2;
       const float x0 = __uint_as_float(sx[e]), x1 = __uint_as_float(sx[e + 1]);
-      const float a0 = fmaf(fabsf(x0), cb, 1.0f), a1 = fmaf(fabsf(x1), cb, 1.0f);
-      const float2 sl = make_float2(copy_sign_bit(lg2_approx(a0), x0),
-                                    copy_sign_bit(lg2_approx(a1), x1));
-      const float2 nlse = pi ? make_float2(nl.z, nl.w) : make_float2(nl.x, nl.y);
-      const float2 ndel = pi ? make_float2(nd.z, nd.w) : make_float2(nd.x, nd.y);
-      const float2 t = __ffma2_rn(n2, sl, nlse);
-      float2 pr = make_float2(ex2_approx(t.x), ex2_approx(t.y));
+      const float2 sl = make_float2(slv[e], slv[e + 1]);
+      float2 pr = prv[e / 2];
       if (MASKED) {
         const int q = q0 + e;
         pr.x = (row_ok && q >= qmin && q < L) ? pr.x : 0.f;
         pr.y = (row_ok && q + 1 >= qmin && q + 1 < L) ? pr.y : 0.f;
       }
+      const float2 ndel = pi ? make_float2(nd.z, nd.w) : make_float2(nd.x, nd.y);
       const float2 dss = __fmul2_rn(pr, __fadd2_rn(make_float2(__uint_as_float(dp[e]),
                                                                __uint_as_float(dp[e + 1])),
                                                    ndel));
-      const float2 w = __fmul2_rn(
-          dss, NRCP ? rcp2_newton(make_float2(a0, a1)) : make_float2(rcp_approx(a0), rcp_approx(a1)));
+      const float2 w = __fmul2_rn(dss, make_float2(rv[e], rv[e + 1]));
       dn_acc[pi] = __ffma2_rn(dss, sl, dn_acc[pi]);
       db_acc[pi] = __ffma2_rn(w, make_float2(x0, x1), db_acc[pi]);
       const float2 dsv = __fmul2_rn(w, nbs2);

@@ -38,6 +38,12 @@ constexpr float kRescaleThreshold = 8.0f;
 // softmax is not bound by the special-function unit alone and the extra work only costs time.
 template <int D>
 constexpr int kEmuPairs = D == 128 ? 1 : 0;
+// D = 64: every element's sign * log2(1 + b|s|) is computed in a first pass over the block (in
+// place of s), the exponentials in a second. Same operations and results as one pass per element
+// pair; measured on B200 the two-pass order is 1% faster at D = 64 (config 2) and 1% slower at
+// D = 128, which keeps one pass.
+template <int D>
+constexpr bool kLogFirst = D == 64;
 
 template <int D>
 struct FwdCfg {
@@ -299,13 +305,33 @@ __global__ void __launch_bounds__(192, 2)
         const float2 t = __ffma2_rn(n2, sl, negm2);
         return emu ? exp2_poly2(t) : make_float2(ex2_approx(t.x), ex2_approx(t.y));
       };
+      auto p_sl = [&](uint32_t s0, uint32_t s1, bool emu) {  // from sign * log2(1 + b|s|)
+        const float2 t =
+            __ffma2_rn(n2, make_float2(__uint_as_float(s0), __uint_as_float(s1)), negm2);
+        return emu ? exp2_poly2(t) : make_float2(ex2_approx(t.x), ex2_approx(t.y));
+      };
+      auto p_of = [&](uint32_t s0, uint32_t s1, bool emu) {
+        if constexpr (kLogFirst<D>)
+          return p_sl(s0, s1, emu);
+        else
+          return p_pair(__uint_as_float(s0), __uint_as_float(s1), emu);
+      };
+      if constexpr (kLogFirst<D>) {
+#pragma unroll
+        for (int c = 0; c < C::BN / 32; ++c) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const float x = __uint_as_float(sr[c][i]);
+            sr[c][i] = __float_as_uint(copy_sign_bit(lg2_approx(fmaf(fabsf(x), cb, 1.0f)), x));
+          }
+        }
+      }
       if (full) {  // no masking code in interior blocks
 #pragma unroll
         for (int c = 0; c < C::BN / 32; ++c) {
 #pragma unroll
           for (int i = 0; i < 32; i += 2) {
-            const float2 pp = p_pair(__uint_as_float(sr[c][i]), __uint_as_float(sr[c][i + 1]),
-                                     ((i >> 1) & 3) < kEmuPairs<D>);
+            const float2 pp = p_of(sr[c][i], sr[c][i + 1], ((i >> 1) & 3) < kEmuPairs<D>);
             rs2 = __fadd2_rn(rs2, pp);
             pk[c >> 1][(c & 1) * 16 + (i >> 1)] = pack2<BF16>(pp.x, pp.y);
           }
@@ -316,8 +342,7 @@ __global__ void __launch_bounds__(192, 2)
 #pragma unroll
           for (int i = 0; i < 32; i += 2) {
             const int col = n0 + c * 32 + i;
-            float2 pp = p_pair(__uint_as_float(sr[c][i]), __uint_as_float(sr[c][i + 1]),
-                               ((i >> 1) & 3) < kEmuPairs<D>);
+            float2 pp = p_of(sr[c][i], sr[c][i + 1], ((i >> 1) & 3) < kEmuPairs<D>);
             pp.x = (col <= lim && row < L) ? pp.x : 0.f;
             pp.y = (col + 1 <= lim && row < L) ? pp.y : 0.f;
             rs2 = __fadd2_rn(rs2, pp);

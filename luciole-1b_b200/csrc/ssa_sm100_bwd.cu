@@ -115,7 +115,8 @@ enum BwdBar : int {
 // accumulate dn/db, and pack P and dS to 16 bits. The fp32 elementwise work runs on element
 // pairs with the packed f32x2 FMA/ADD/MUL instructions (half the issue slots); lrow / drow hold
 // -lse and -delta so both subtractions fold into packed FMA / ADD. MASKED adds the causal /
-// bounds test (valid iff the row is in range and qmin <= q < L). NRCP takes 1/(1+u) from
+// bounds test (valid iff the row is in range and qmin <= q < L), applied to the exponent: an
+// invalid element gets t = -inf and ex2.approx returns +0 for it. NRCP takes 1/(1+u) from
 // Newton steps on the FMA pipe instead of the special-function unit.
 template <int W, bool BF16, bool MASKED, bool NRCP>
 __device__ __forceinline__ void bwd_chunk(const uint32_t (&sx)[W], const uint32_t (&dp)[W],
@@ -147,7 +148,12 @@ __device__ __forceinline__ void bwd_chunk(const uint32_t (&sx)[W], const uint32_
     for (int pi = 0; pi < 2; ++pi) {
       const int e = e4 * 4 + pi * 2;
       const float2 nlse = pi ? make_float2(nl.z, nl.w) : make_float2(nl.x, nl.y);
-      const float2 t = __ffma2_rn(n2, make_float2(slv[e], slv[e + 1]), nlse);
+      float2 t = __ffma2_rn(n2, make_float2(slv[e], slv[e + 1]), nlse);
+      if (MASKED) {
+        const int q = q0 + e;
+        t.x = (row_ok && q >= qmin && q < L) ? t.x : -INFINITY;
+        t.y = (row_ok && q + 1 >= qmin && q + 1 < L) ? t.y : -INFINITY;
+      }
       prv[e / 2] = make_float2(ex2_approx(t.x), ex2_approx(t.y));
     }
   }
@@ -159,12 +165,7 @@ __device__ __forceinline__ void bwd_chunk(const uint32_t (&sx)[W], const uint32_
       const int e = e4 * 4 + pi * 2;
       const float x0 = __uint_as_float(sx[e]), x1 = __uint_as_float(sx[e + 1]);
       const float2 sl = make_float2(slv[e], slv[e + 1]);
-      float2 pr = prv[e / 2];
-      if (MASKED) {
-        const int q = q0 + e;
-        pr.x = (row_ok && q >= qmin && q < L) ? pr.x : 0.f;
-        pr.y = (row_ok && q + 1 >= qmin && q + 1 < L) ? pr.y : 0.f;
-      }
+      const float2 pr = prv[e / 2];
       const float2 ndel = pi ? make_float2(nd.z, nd.w) : make_float2(nd.x, nd.y);
       const float2 dss = __fmul2_rn(pr, __fadd2_rn(make_float2(__uint_as_float(dp[e]),
                                                                __uint_as_float(dp[e + 1])),

@@ -92,7 +92,7 @@ def score_elements() -> float:
 
 # ncu DRAM traffic (read+write bytes) per launch of the dominant kernel (bwd_sm100_kernel),
 # taken from one ncu capture of this workload; None when no capture matches the current kernel.
-NCU_TRAFFIC_BYTES = 1.513e9  # bwd_sm100_kernel, one ncu capture at config 2: dram read + write
+NCU_TRAFFIC_BYTES = 1.516e9  # bwd_sm100_kernel, one ncu capture at config 2: dram read + write
 
 
 def flops_per_rank() -> float:

@@ -305,9 +305,10 @@ __global__ void __launch_bounds__(192, 2)
         const float2 t = __ffma2_rn(n2, sl, negm2);
         return emu ? exp2_poly2(t) : make_float2(ex2_approx(t.x), ex2_approx(t.y));
       };
-      auto p_sl = [&](uint32_t s0, uint32_t s1, bool emu) {  // from sign * log2(1 + b|s|)
-        const float2 t =
-            __ffma2_rn(n2, make_float2(__uint_as_float(s0), __uint_as_float(s1)), negm2);
+      auto p_sl = [&](uint32_t s0, uint32_t s1, bool emu, bool v0 = true, bool v1 = true) {
+        float2 t = __ffma2_rn(n2, make_float2(__uint_as_float(s0), __uint_as_float(s1)), negm2);
+        t.x = v0 ? t.x : -INFINITY;  // ex2.approx(-inf) = +0
+        t.y = v1 ? t.y : -INFINITY;
         return emu ? exp2_poly2(t) : make_float2(ex2_approx(t.x), ex2_approx(t.y));
       };
       auto p_of = [&](uint32_t s0, uint32_t s1, bool emu) {
@@ -342,9 +343,16 @@ __global__ void __launch_bounds__(192, 2)
 #pragma unroll
           for (int i = 0; i < 32; i += 2) {
             const int col = n0 + c * 32 + i;
-            float2 pp = p_of(sr[c][i], sr[c][i + 1], ((i >> 1) & 3) < kEmuPairs<D>);
-            pp.x = (col <= lim && row < L) ? pp.x : 0.f;
-            pp.y = (col + 1 <= lim && row < L) ? pp.y : 0.f;
+            float2 pp;
+            if constexpr (kLogFirst<D>) {
+              pp = p_sl(sr[c][i], sr[c][i + 1], false, col <= lim && row < L,
+                        col + 1 <= lim && row < L);
+            } else {
+              pp = p_pair(__uint_as_float(sr[c][i]), __uint_as_float(sr[c][i + 1]),
+                          ((i >> 1) & 3) < kEmuPairs<D>);
+              pp.x = (col <= lim && row < L) ? pp.x : 0.f;
+              pp.y = (col + 1 <= lim && row < L) ? pp.y : 0.f;
+            }
             rs2 = __fadd2_rn(rs2, pp);
             pk[c >> 1][(c & 1) * 16 + (i >> 1)] = pack2<BF16>(pp.x, pp.y);
           }

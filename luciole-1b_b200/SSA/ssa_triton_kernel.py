@@ -143,7 +143,7 @@ def ssa_flash_attn_backward(q, k, v, out, dout, m, softmax_scale, ssa_n, ssa_b, 
     prob = _problem(q, Hkv, softmax_scale, n, b, per_head, causal, B, N)
     fam = lib.ssa_attn_kernel_family(ctypes.byref(prob))
     q, k, v, dout = _prep(q, fam), _prep(k, fam), _prep(v, fam), _prep(dout, fam)
-    out = out if out.stride(-1) == 1 else out.contiguous()
+    out = _prep(out, fam)
     dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
     dn, db = _param_grad_pair(n, q.device)
     ws_bytes = lib.ssa_attn_bwd_workspace_size(ctypes.byref(prob))
@@ -185,12 +185,6 @@ def _check_padded(cu_seqlens, cu_seqlens_padded):
     return cu_seqlens_padded
 
 
-def _prep3(t, fam):
-    if t.stride(-1) != 1 or (fam == 1 and not _tma_ok(t)):
-        return t.contiguous()
-    return t
-
-
 def ssa_flash_attn_varlen_forward(q, k, v, cu_seqlens, max_seqlen, softmax_scale, ssa_n, ssa_b,
                                   causal=True, cu_seqlens_padded=None):
     """Packed documents: q [T, Hq, D], k/v [T, Hkv, D], cu_seqlens int32 [ndoc+1].
@@ -208,7 +202,7 @@ def ssa_flash_attn_varlen_forward(q, k, v, cu_seqlens, max_seqlen, softmax_scale
     prob = _problem(q, Hkv, softmax_scale, n, b, per_head, causal, ndoc, T,
                     cu_seqlens, max_seqlen, cu_pad)
     fam = lib.ssa_attn_kernel_family(ctypes.byref(prob))
-    q, k, v = _prep3(q, fam), _prep3(k, fam), _prep3(v, fam)
+    q, k, v = _prep(q, fam), _prep(k, fam), _prep(v, fam)
     alloc = torch.zeros if cu_pad is not None else torch.empty
     out = alloc(q.shape, dtype=q.dtype, device=q.device)
     lse = torch.empty((Hq, T), device=q.device, dtype=torch.float32)
@@ -232,8 +226,8 @@ def ssa_flash_attn_varlen_backward(q, k, v, out, dout, lse, cu_seqlens, max_seql
     prob = _problem(q, Hkv, softmax_scale, n, b, per_head, causal, ndoc, T,
                     cu_seqlens, max_seqlen, cu_pad)
     fam = lib.ssa_attn_kernel_family(ctypes.byref(prob))
-    q, k, v, dout = _prep3(q, fam), _prep3(k, fam), _prep3(v, fam), _prep3(dout, fam)
-    out = out if out.stride(-1) == 1 else out.contiguous()
+    q, k, v, dout = _prep(q, fam), _prep(k, fam), _prep(v, fam), _prep(dout, fam)
+    out = _prep(out, fam)
     alloc = torch.zeros if cu_pad is not None else torch.empty
     dq = alloc(q.shape, dtype=q.dtype, device=q.device)
     dk = alloc(k.shape, dtype=k.dtype, device=k.device)

@@ -67,9 +67,11 @@ def _tma_ok(t: torch.Tensor) -> bool:
 
 
 def _prep(t: torch.Tensor, family: int) -> torch.Tensor:
-    """Unit stride on D always; 16-byte-aligned strides for the TMA (tensor-core) family."""
+    """Unit stride on D always; a 16-byte-aligned base and B/H/N strides for the TMA
+    (tensor-core) family. Anything else is copied into fresh storage (``contiguous()`` would
+    keep a misaligned base of an already-contiguous view)."""
     if t.stride(-1) != 1 or (family == 1 and not _tma_ok(t)):
-        return t.contiguous()
+        return t.clone(memory_format=torch.contiguous_format)
     return t
 
 

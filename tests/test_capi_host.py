@@ -170,3 +170,25 @@ def test_packed_params_validation_before_any_kernel():
         mod(q, kv, kv, None, packed_seq_params=bad)
     assert _same(None, cu) and _same(cu, cu) and _same(cu.clone(), cu)
     assert not _same(torch.tensor([0, 5, 10], dtype=torch.int32), cu)
+
+
+def test_layout_rule_of_the_wrappers():
+    """Which layouts the wrappers hand to the kernels as they are and which they copy: unit D
+    stride always; for the TMA (tensor-core) family also a 16-byte-aligned base and B/H/N
+    strides. Megatron's [S, B, H, D] permuted view passes untouched."""
+    from SSA.ssa_triton_kernel import _prep, _tma_ok
+    x = torch.zeros(2, 4, 64, 64, dtype=torch.bfloat16)
+    megatron = torch.zeros(64, 2, 4, 64, dtype=torch.bfloat16).permute(1, 2, 0, 3)
+    odd_rows = torch.zeros(2, 4, 64, 65, dtype=torch.bfloat16)[..., :64]  # 130-byte rows
+    odd_base = torch.zeros(2 * 4 * 64 * 64 + 1, dtype=torch.bfloat16)[1:].view(2, 4, 64, 64)
+    d_strided = torch.zeros(2, 4, 64, 128, dtype=torch.bfloat16)[..., ::2]
+    assert _tma_ok(x) and _tma_ok(megatron)
+    assert not _tma_ok(odd_rows) and not _tma_ok(odd_base) and not _tma_ok(d_strided)
+    for t in (x, megatron):
+        assert _prep(t, 1) is t and _prep(t, 0) is t
+    for t in (odd_rows, odd_base):
+        c = _prep(t, 1)
+        assert c is not t and c.is_contiguous() and torch.equal(c, t) and _tma_ok(c)
+        assert _prep(t, 0) is t  # the generic kernels only need a unit D stride
+    c = _prep(d_strided, 0)
+    assert c is not d_strided and c.stride(-1) == 1 and torch.equal(c, d_strided)

@@ -69,20 +69,24 @@ UNIT = "TFLOP/s"
 DOC_LENS = None  # varlen document lengths (c3)
 
 
+def c3_doc_lengths(total: int = 65536, seed: int = 3) -> list:
+    """Config 3's packing: document lengths drawn seeded and uniform in [128, 4096] until they
+    sum to `total` tokens (the last one clipped). The GPU parity tests check the same packing."""
+    g = torch.Generator().manual_seed(seed)
+    lens, tot = [], 0
+    while tot < total:
+        L = min(int(torch.randint(128, 4097, (1,), generator=g)), total - tot)
+        lens.append(L)
+        tot += L
+    return lens
+
+
 def select_config(name: str) -> None:
     global CFG, B, HQ, HKV, S, D, WORKLOAD, METRIC, DOC_LENS
     CFG = CONFIGS[name]
     B, HQ, HKV, S, D = CFG["B"], CFG["HQ"], CFG["HKV"], CFG["S"], CFG["D"]
     WORKLOAD, METRIC = CFG["workload"], CFG["metric"]
-    if CFG["varlen"]:
-        g = torch.Generator().manual_seed(3)
-        lens, tot = [], 0
-        while tot < S:
-            L = int(torch.randint(128, 4097, (1,), generator=g))
-            L = min(L, S - tot)
-            lens.append(L)
-            tot += L
-        DOC_LENS = lens
+    DOC_LENS = c3_doc_lengths(S) if CFG["varlen"] else None
 
 
 def score_elements() -> float:
@@ -90,9 +94,58 @@ def score_elements() -> float:
         return float(HQ * sum(L * L // 2 for L in DOC_LENS))
     return float(B * HQ * (S * S // 2 if CAUSAL else S * S))
 
-# ncu DRAM traffic (read+write bytes) per launch of the dominant kernel (bwd_sm100_kernel),
-# taken from one ncu capture of this workload; None when no capture matches the current kernel.
-NCU_TRAFFIC_BYTES = 1.516e9  # bwd_sm100_kernel, one ncu capture at config 2: dram read + write
+def shard_score_elements(n_seq: int, n_qheads: int) -> float:
+    """Score elements of a shard holding n_seq sequences (all documents when packed) x n_qheads."""
+    if DOC_LENS is not None:
+        return float(n_qheads * sum(L * L // 2 for L in DOC_LENS))
+    return float(n_seq * n_qheads * (S * S // 2 if CAUSAL else S * S))
+
+
+def strong_shard(world: int, rank: int):
+    """This rank's part of the config's fixed batch for strong scaling: the balanced contiguous
+    range of (batch, kv-head) units that SSA.shard.unit_shard assigns, as (batch slice, kv-head
+    slice). Needs the range to be a rectangle: world divides B (whole sequences) or world is a
+    multiple of B whose share of each sequence divides Hkv (a kv-head range of one sequence)."""
+    from SSA.shard import unit_shard
+    units = unit_shard(B, HKV, world, rank)
+    bs = sorted({u[0] for u in units})
+    hs = sorted({u[1] for u in units})
+    rect = (len(units) == len(bs) * len(hs) and bs == list(range(bs[0], bs[-1] + 1))
+            and hs == list(range(hs[0], hs[-1] + 1)))
+    if not units or not rect:
+        raise SystemExit(f"--scaling strong: {world} ranks do not split B={B} x Hkv={HKV} into "
+                         f"rectangles of (batch, kv-head) units; use --scaling weak")
+    return slice(bs[0], bs[-1] + 1), slice(hs[0], hs[-1] + 1)
+
+
+# DRAM traffic per launch of the dominant kernel (bwd_sm100_kernel) comes from the committed ncu
+# summary of this workload, and only while the kernel source is the one that capture measured:
+# the summary's "bench-traffic:" line carries the source file's sha256 prefix and the bytes.
+TRAFFIC_PROFILE = REPO / "profiles" / "ssa_bwd_sm100_config2.md"
+TRAFFIC_SOURCE = REPO / "luciole-1b_b200" / "csrc" / "ssa_sm100_bwd.cu"
+
+
+def ncu_traffic():
+    """(dram bytes per launch or None, note)."""
+    import hashlib
+    import re
+    if not TRAFFIC_PROFILE.exists():
+        return None, "no ncu summary committed"
+    m = re.search(r"^bench-traffic:.*sha256_16=([0-9a-f]{16}).*dram_bytes=([0-9.e+]+)",
+                  TRAFFIC_PROFILE.read_text(), re.M)
+    if not m:
+        return None, "ncu summary has no bench-traffic line"
+    sha = hashlib.sha256(TRAFFIC_SOURCE.read_bytes()).hexdigest()[:16]
+    if sha != m.group(1):
+        return None, "stale: the ncu capture measured an earlier ssa_sm100_bwd.cu"
+    return float(m.group(2)), f"ncu capture of ssa_sm100_bwd.cu sha256 {sha}"
+
+
+REFERENCE_TRITON = {
+    "unavailable": "the reference's Triton SSA kernels cannot be timed on the B200 box: the "
+                   "reference is not an installable package (pip: 'Neither setup.py nor "
+                   "pyproject.toml found', so baseline/_ref stays empty) and its Python "
+                   "sources may not travel to the box or be copied into this repository"}
 
 
 def flops_per_rank() -> float:
@@ -110,15 +163,15 @@ SFU_OPS_PER_ELEMENT = 4
 SFU_OPS_PER_CLK_SM = 16
 
 
-def sfu_floor(ms_per_step: float) -> dict:
-    """The special-function floor of one step (algorithmic elements, max SM clock) and the
-    fraction of it the measured step reaches."""
+def sfu_floor(ms_per_step: float, elements: float) -> dict:
+    """The special-function floor of one step over `elements` score elements on one GPU
+    (algorithmic elements, max SM clock) and the fraction of it the measured step reaches."""
     sms = torch.cuda.get_device_properties(0).multi_processor_count if torch.cuda.is_available() else 148
     mhz = 1965.0
     p = REPO / "MEASURED_PEAKS.json"
     if p.exists():
         mhz = float(json.loads(p.read_text()).get("sm_max_mhz", mhz))
-    ops = SFU_OPS_PER_ELEMENT * score_elements()
+    ops = SFU_OPS_PER_ELEMENT * elements
     peak = SFU_OPS_PER_CLK_SM * sms * mhz * 1e6
     floor_ms = ops / peak * 1e3
     return {"ops_per_step": ops, "peak_ops_per_s": peak, "floor_ms": floor_ms,
@@ -249,18 +302,25 @@ def run_reference(args):
     if rank != 0:
         return
     threads = os.cpu_count() or 1
-    vals = []
+    vals, secs = [], []
+    fl = 0.0
     for i in range(args.warmup + args.steps):
-        v, _, _, _ = _one_ref_step(threads)
+        v, el, fl, _ = _one_ref_step(threads)
         if i >= args.warmup:
             vals.append(v)
+            secs.append(el)
     val = statistics.median(vals)
-    sample = (f"one q-head of one sequence (S={min(S, 2048)}, D={D}, causal) per step, fp32 "
-              f"eager restatement of the reference's SSA path with autograd")
+    step_s = statistics.median(secs)
+    sample = (f"one q-head of one sequence (S={min(S, 2048)}, D={D}, causal) per step: "
+              f"{fl:.4g} FLOPs in a median {step_s * 1e3:.1f} ms; fp32 eager restatement of the "
+              f"reference's SSA path with autograd, {threads} threads")
     line = {"impl": "reference", "metric": METRIC, "value": val, "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-            "config": {"workload": WORKLOAD, "global_batch": B * world, "seq_len": S},
+            "ms_per_step": step_s * 1e3, "sample_flops_per_step": fl,
+            # the whole config's work at this rate (the sample is a bounded slice of it)
+            "config_ms_equivalent": flops_per_rank() / (val * 1e12) * 1e3,
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "global_batch": B, "seq_len": S},
             "cpu_baseline": {"value": val, "unit": UNIT, "cores": threads, "kind": "port",
                              "sample": sample},
             "e2e": {"value": val, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -395,6 +455,10 @@ def main():
     ap.add_argument("--cp", action="store_true",
                     help="context-parallel ring over the ranks (strong scaling of one sequence; "
                          "use with --config c4 under torchrun)")
+    ap.add_argument("--scaling", default="strong", choices=["strong", "weak"],
+                    help="strong (default): the config's fixed batch is split across the ranks "
+                         "by (batch, kv-head) units; weak: every rank runs the whole config on "
+                         "its own data (global batch = N x the config's)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     if args.config == "c5":
@@ -421,7 +485,27 @@ def main():
 
     from SSA.ssa_triton_kernel import (ssa_flash_attn_varlen_backward,
                                        ssa_flash_attn_varlen_forward)
-    q_h, k_h, v_h, do_h, n_h = make_inputs(dev, seed=rank)
+    strong = args.scaling == "strong" and not args.cp
+    if strong:
+        # The config's fixed batch, split by (batch, kv-head) units: every rank builds the same
+        # seeded inputs and keeps its own units (a rectangle of sequences x kv-heads).
+        bsl, hsl = strong_shard(world, rank)
+        g = HQ // HKV
+        qsl = slice(hsl.start * g, hsl.stop * g)
+        q_h, k_h, v_h, do_h, n_h = make_inputs(dev, seed=0)
+        if DOC_LENS is not None:
+            q_h, do_h = (t[:, qsl].contiguous() for t in (q_h, do_h))
+            k_h, v_h = (t[:, hsl].contiguous() for t in (k_h, v_h))
+        else:
+            q_h, do_h = (t[bsl, qsl].contiguous() for t in (q_h, do_h))
+            k_h, v_h = (t[bsl, hsl].contiguous() for t in (k_h, v_h))
+        n_h = n_h[qsl].contiguous()
+        shard_elems = shard_score_elements(bsl.stop - bsl.start, qsl.stop - qsl.start)
+    else:
+        q_h, k_h, v_h, do_h, n_h = make_inputs(dev, seed=rank)
+        qsl = slice(0, HQ)
+        shard_elems = score_elements()
+    all_heads = qsl.stop - qsl.start == HQ
     q, k, v, do = (t.to(dev) for t in (q_h, k_h, v_h, do_h))
     n = n_h.to(dev)
     bb = torch.tensor(SSA_B, device=dev)
@@ -464,11 +548,23 @@ def main():
         def attn_bwd(q_, k_, v_, o_, do_, m_):
             return ring_ssa_backward(q_, k_, v_, o_, do_, m_, scale, n, bb)
 
+    dnb_full = torch.zeros(HQ + 1, device=dev, dtype=torch.float32)
+
+    def reduce_dn_db(dn_, db_, async_op=False):
+        """Sum dn / db over the ranks: in place when this rank holds every q-head (dn and db are
+        adjacent in one buffer), else through a full-width [Hq + 1] buffer."""
+        if all_heads:
+            return allreduce_ssa_param_grads(dn_, db_, async_op=async_op)
+        dnb_full.zero_()
+        dnb_full[qsl].copy_(dn_)
+        dnb_full[HQ:].copy_(db_.reshape(1))
+        return dist.all_reduce(dnb_full, async_op=async_op)
+
     def step():
         out, m = attn_fwd(q, k, v)
         dq, dk, dv, dn, db = attn_bwd(q, k, v, out, do, m)
         if reduce_params:
-            allreduce_ssa_param_grads(dn, db)
+            reduce_dn_db(dn, db)
         return out, dq, dk, dv, dn, db
 
     def barrier():
@@ -499,7 +595,7 @@ def main():
             e2.record(st)
             if reduce_params:
                 # in place on the (adjacent) dn/db; overlaps the next step's forward
-                pending.append(allreduce_ssa_param_grads(dn, db, async_op=True))
+                pending.append(reduce_dn_db(dn, db, async_op=True))
         for w in pending:  # every reduction finishes inside the timed region
             w.wait()
         stop.record(st)
@@ -512,7 +608,8 @@ def main():
         t = torch.tensor([ms], device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
-    job_flops = flops_per_rank() * (1 if args.cp else world)  # cp: one sequence split
+    # strong / cp: the config's fixed work split over the ranks; weak: every rank runs it all
+    job_flops = flops_per_rank() * (world if (not strong and not args.cp) else 1)
     value = job_flops / (ms * 1e-3) / 1e12
 
     # ---- e2e: through the public API with pinned host buffers, copies inside the timed region.
@@ -525,7 +622,8 @@ def main():
     q_p, k_p, v_p, do_p = (t.pin_memory() for t in (q_h, k_h, v_h, do_h))
     outs_p = [[torch.empty(q_h.shape, dtype=torch.bfloat16).pin_memory() for _ in range(2)] +
               [torch.empty(k_h.shape, dtype=torch.bfloat16).pin_memory() for _ in range(2)] +
-              [torch.empty(HQ + 1, dtype=torch.float32).pin_memory()] for _ in range(2)]
+              [torch.empty(n_h.numel() + 1, dtype=torch.float32).pin_memory()]
+              for _ in range(2)]
     dev_in = [[torch.empty_like(t, device=dev) for t in (q_p, k_p, v_p, do_p)] for _ in range(2)]
     h2d = sum(t.numel() * t.element_size() for t in (q_p, k_p, v_p, do_p))
     d2h = sum(t.numel() * t.element_size() for t in outs_p[0])
@@ -554,7 +652,7 @@ def main():
         out_, m_ = attn_fwd(qd, kd, vd)
         dq_, dk_, dv_, dn_, db_ = attn_bwd(qd, kd, vd, out_, dod, m_)
         if reduce_params:
-            allreduce_ssa_param_grads(dn_, db_)
+            reduce_dn_db(dn_, db_)
         res = torch.cat([dn_.reshape(-1), db_.reshape(1)])
         ev = torch.cuda.Event()
         ev.record(st)
@@ -589,7 +687,10 @@ def main():
 
     status = _lib.load().ssa_device_status(_lib.stream_ptr(dev))
     peak_tf, _, peak_kind = measured_peaks()
-    achieved = flops_bwd_per_rank() / (world if args.cp else 1) / (t_bwd * 1e-3) / 1e12
+    # this rank's own backward work over its own backward time
+    rank_elems = score_elements() / world if args.cp else shard_elems
+    traffic, traffic_note = ncu_traffic()
+    achieved = 10.0 * D * rank_elems / (t_bwd * 1e-3) / 1e12
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         threads = os.cpu_count() or 1
@@ -601,14 +702,18 @@ def main():
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True,
-            "scaling": "strong" if args.cp else "weak", "vs_baseline": None, "dtype": "bf16",
+            "scaling": "weak" if not (strong or args.cp) else "strong", "vs_baseline": None,
+            "dtype": "bf16",
             "data": "synthetic",
-            "config": {"workload": WORKLOAD, "global_batch": B * (1 if args.cp else world),
+            "config": {"workload": WORKLOAD,
+                       "global_batch": B * (world if not (strong or args.cp) else 1),
                        "seq_len": S,
                        "heads_q": HQ, "heads_kv": HKV, "head_dim": D, "causal": CAUSAL,
                        "parallelism": (f"context-parallel ring x{world} (zig-zag, NCCL P2P)"
                                        if args.cp else
-                                       f"batch-shard x{world} (weak), dn/db all-reduce"),
+                                       (f"(batch, kv-head) unit shard x{world} of the fixed "
+                                        f"batch (strong), dn/db all-reduce" if strong else
+                                        f"batch-shard x{world} (weak), dn/db all-reduce")),
                        "l2": "inputs larger than L2 (~300 MB resident per rank)"},
             "fwd_ms": t_fwd, "bwd_ms": t_bwd,
             "frac_of_peak": value / world / peak_tf,
@@ -617,10 +722,12 @@ def main():
             "roofline": {"bound": "tensor", "kernel": "ssa_attn_bwd call (dominant)",
                          "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
                          "frac": achieved / peak_tf, "peak_kind": f"{peak_kind} bf16 burst",
-                         "traffic": NCU_TRAFFIC_BYTES if args.config == "c2" else None,
+                         "traffic": traffic if args.config == "c2" else None,
+                         "traffic_note": traffic_note if args.config == "c2" else None,
                          # what bounds SSA at D = 64: the special-function unit (lg2 / ex2)
-                         # (context parallelism: each rank has 1/world of the job's elements)
-                         "sfu": sfu_floor(ms * (world if args.cp else 1))},
+                         # per rank: its own score elements over the max-over-ranks step time
+                         "sfu": sfu_floor(ms, rank_elems)},
+            "reference_triton": REFERENCE_TRITON,
             "cpu_baseline": cpu,
             "clocks": clk.summary(),
             "gpu_launches": launches,

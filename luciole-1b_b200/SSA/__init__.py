@@ -5,3 +5,5 @@
 #   ssa_triton_attention.py     - Megatron-compatible core-attention module
 #   ssa_triton_layer_specs.py   - Megatron GPT layer spec using the module
 # The module names are the reference's; the kernels are hand-written CUDA, not Triton.
+
+from .ssa_triton_kernel import check_device_status  # noqa: E402,F401

@@ -29,6 +29,7 @@ from . import _lib
 __all__ = [
     "ssa_flash_attn_forward", "ssa_flash_attn_backward", "ssa_flash_attn_varlen_forward",
     "ssa_flash_attn_varlen_backward", "warmup_ssa_triton_kernels", "kernel_family",
+    "check_device_status",
 ]
 
 
@@ -89,6 +90,23 @@ def _check_qkv(q, k, v):
     if Hq % Hkv != 0:
         raise ValueError(f"Hq={Hq} must be divisible by Hkv={Hkv}")
     return B, Hq, Hkv, N, D
+
+
+def check_device_status(device=None) -> None:
+    """Raise ``SSAKernelError`` (code ``SSA_ERR_DEVICE_TIMEOUT``) if a bounded device-side wait of
+    the sm_100a kernels expired on ``device`` (default: the current CUDA device) since the last
+    check. Reads and clears the device status word, synchronising the current stream.
+
+    Every wait inside the tensor-core kernels gives up after about a second instead of hanging
+    the GPU. From then on, until this check clears the status, those kernels skip their work and
+    write NaN into every output (out, m, dq, dk, dv, dn, db), so a training loop that never calls
+    this still sees the failure as NaN (the reference's DDP ``check_for_nan_in_grad`` trips on
+    it). Call it where a host synchronisation is acceptable, e.g. once per optimizer step.
+    """
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    lib = _lib.load()
+    rc = lib.ssa_device_status(_lib.stream_ptr(dev))
+    _lib.check(rc)
 
 
 def kernel_family(q: torch.Tensor, softmax_scale: float = 1.0) -> int:

@@ -1,51 +1,37 @@
 """Megatron GPT layer spec with SSA core attention (drop-in for the reference's
 ``SSA.ssa_triton_layer_specs``, training/train/train_ssa_triton/SSA/ssa_triton_layer_specs.py).
 
-Same function names and signatures. Megatron-core is imported lazily, so importing this
-module works without it; building a spec needs it.
+Same layer-spec function and signature. Megatron-core is imported lazily, so importing this
+module works without it; building a spec needs it. The residual bias-dropout-add is Megatron's
+own (``megatron.core.fusions.fused_bias_dropout.get_bias_dropout_add``), optionally compiled with
+``torch.compile`` as the reference does (``SSA_TRITON_COMPILE_BDA``, default on).
 """
 
 from __future__ import annotations
 
+import functools
 import os
 from typing import Optional
 
 from .ssa_triton_attention import SSATritonAttention
 
 
-def get_bias_dropout_add(training, fused_bias_dropout_add):
-    """Bias-dropout-add function factory expected by TransformerLayer (reference :27-39)."""
+def _compiled_bda_factory(training, fused):
+    """Bias-dropout-add factory for ``use_compiled_bda`` (the reference compiles its unfused
+    bias-dropout-add with ``torch.compile``, ssa_triton_layer_specs.py:45-60): Megatron's own
+    unfused function for ``training``, compiled once per flag."""
+    return _compiled_bda(bool(training))
+
+
+@functools.lru_cache(maxsize=None)
+def _compiled_bda(training: bool):
     import torch
-
-    def bias_dropout_add(x_with_bias, residual, prob):
-        x, bias = x_with_bias
-        if bias is not None:
-            x = x + bias
-        if training and prob > 0.0:
-            x = torch.nn.functional.dropout(x, p=prob, training=True)
-        return x + residual
-
-    return bias_dropout_add
-
-
-_compiled_bda_cache = {}
-
-
-def get_compiled_bias_dropout_add(training, fused_bias_dropout_add):
-    """torch.compile'd bias-dropout-add (reference :45-60); falls back to eager on failure."""
-    import torch
-
-    key = (training,)
-    if key in _compiled_bda_cache:
-        return _compiled_bda_cache[key]
-    fn = get_bias_dropout_add(training, fused_bias_dropout_add)
+    from megatron.core.fusions.fused_bias_dropout import get_bias_dropout_add
+    eager = get_bias_dropout_add(training, False)
     try:
-        compiled = torch.compile(fn, mode="reduce-overhead")
-        _compiled_bda_cache[key] = compiled
-        return compiled
-    except Exception:
-        _compiled_bda_cache[key] = fn
-        return fn
+        return torch.compile(eager, mode="reduce-overhead")
+    except Exception:  # no compiler backend here: the eager function computes the same thing
+        return eager
 
 
 def get_ssa_triton_gpt_layer_spec(num_experts: Optional[int] = None,
@@ -64,9 +50,11 @@ def get_ssa_triton_gpt_layer_spec(num_experts: Optional[int] = None,
     from megatron.core.transformer.transformer_layer import (TransformerLayer,
                                                              TransformerLayerSubmodules)
 
+    from megatron.core.fusions.fused_bias_dropout import get_bias_dropout_add
+
     if use_compiled_bda is None:
         use_compiled_bda = os.environ.get("SSA_TRITON_COMPILE_BDA", "1") != "0"
-    bda_factory = get_compiled_bias_dropout_add if use_compiled_bda else get_bias_dropout_add
+    bda_factory = _compiled_bda_factory if use_compiled_bda else get_bias_dropout_add
     mlp = _get_mlp_module_spec(num_experts=num_experts, moe_grouped_gemm=moe_grouped_gemm)
     core = ModuleSpec(module=SSATritonAttention,
                       params={"ssa_n": ssa_n, "ssa_b": ssa_b, "learnable_ssa": learnable_ssa,

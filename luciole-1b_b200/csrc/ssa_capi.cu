@@ -219,6 +219,7 @@ int abi_validate_problem(const ssa_problem_t* pr) {
   g_err[0] = 0;
   return check_problem(pr);
 }
+int abi_check_tensor(const ssa_tensor_t& t, const char* name) { return check_tensor(t, name); }
 Problem abi_to_problem(const ssa_problem_t* pr) { return to_problem(pr); }
 int abi_bind_device(const void* ptr, const char* name) { return bind_device(ptr, name); }
 int abi_error(int code, const char* fmt, ...) {
@@ -363,11 +364,13 @@ int ssa_selftest_device_timeout(uint64_t wait_cycles, void* stream) {
 }
 
 int ssa_device_status(void* stream) {
+  g_err[0] = 0;
   int dev = -1;
   if (cudaStreamGetDevice(static_cast<cudaStream_t>(stream), &dev) == cudaSuccess)
     cudaSetDevice(dev);
   else
     cudaGetLastError();
+  cudaGetDevice(&dev);
   unsigned int* ptr = device_status_ptr();
   if (!ptr) return fail(SSA_ERR_CUDA, "cannot resolve the device status word");
   unsigned int h = 0;
@@ -376,7 +379,12 @@ int ssa_device_status(void* stream) {
       cudaMemsetAsync(ptr, 0, sizeof(h), st) != cudaSuccess ||
       cudaStreamSynchronize(st) != cudaSuccess)
     return fail(SSA_ERR_CUDA, "reading the device status word failed");
-  return h ? SSA_ERR_DEVICE_TIMEOUT : SSA_OK;
+  if (h)
+    return fail(SSA_ERR_DEVICE_TIMEOUT,
+                "a bounded device-side wait expired on device %d; the sm_100a kernels launched "
+                "since then skipped their work and wrote NaN outputs (status now cleared)",
+                dev);
+  return SSA_OK;
 }
 
 }  // extern "C"

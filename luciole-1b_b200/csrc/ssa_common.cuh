@@ -73,6 +73,31 @@ __device__ __forceinline__ float load_n(const Problem& p, int hq) {
   return __ldg(p.n_ptr + (p.n_per_head ? hq : 0));
 }
 
+// Quiet NaN written into the outputs of a kernel that skipped its work because a bounded device
+// wait expired (in this launch or an earlier one): a caller that never reads the status word still
+// sees the failure as NaN in out / lse / dq / dk / dv / dn / db instead of stale memory.
+constexpr uint32_t kNaNBf16x2 = 0x7FC07FC0u, kNaNF16x2 = 0x7E007E00u;
+__device__ __forceinline__ float nan_f32() { return __uint_as_float(0x7FC00000u); }
+
+// NaN into rows [row0, row1) (every head dim) of head h of sequence z of a 16-bit tensor whose
+// rows are 16-byte aligned (true on the TMA path), and into the matching fp32 row statistics when
+// stat != nullptr. Called by every thread of the block.
+template <bool BF16>
+__device__ __forceinline__ void nan_fill_rows16(const TensorRef& t, const Problem& p, int z, int h,
+                                                int seq_start, int row0, int row1, float* stat) {
+  const uint32_t w = BF16 ? kNaNBf16x2 : kNaNF16x2;
+  const int per_row = p.D / 8;  // 16-byte chunks per row
+  const int total = (row1 - row0) * per_row;
+  for (int i = threadIdx.x; i < total; i += blockDim.x) {
+    const int r = row0 + i / per_row, c = i - (i / per_row) * per_row;
+    uint16_t* rowp = reinterpret_cast<uint16_t*>(t.ptr) + row_offset(t, p, z, h, seq_start, r);
+    reinterpret_cast<uint4*>(rowp)[c] = make_uint4(w, w, w, w);
+  }
+  if (stat)
+    for (int r = row0 + (int)threadIdx.x; r < row1; r += blockDim.x)
+      stat[stat_offset(p, z, h, seq_start, r)] = nan_f32();
+}
+
 template <typename T> __device__ __forceinline__ float to_f32(T x);
 template <> __device__ __forceinline__ float to_f32<float>(float x) { return x; }
 template <> __device__ __forceinline__ float to_f32<__half>(__half x) { return __half2float(x); }

@@ -41,6 +41,8 @@ void note_launches(int n);
 // failure), conversion to the device-side Problem, and recording an error message that
 // ssa_last_error() then returns.
 int abi_validate_problem(const ssa_problem_t* pr);
+// Non-NULL pointer and non-negative B/H/N strides (the rule every entry point applies).
+int abi_check_tensor(const ssa_tensor_t& t, const char* name);
 Problem abi_to_problem(const ssa_problem_t* pr);
 int abi_error(int code, const char* fmt, ...);
 // One CTA waiting on an mbarrier nobody completes, with a bounded wait of `cycles` (self-test of

@@ -67,9 +67,12 @@ extern "C" int ssa_attn_bwd_noalloc(const ssa_problem_t* pr, ssa_tensor_t q, ssa
                                     ssa_tensor_t dv, float* dn, float* db, void* stream) {
   int rc = abi_validate_problem(pr);
   if (rc != SSA_OK) return rc;
-  if (!q.ptr || !k.ptr || !v.ptr || !out.ptr || !dout.ptr || !dq.ptr || !dk.ptr || !dv.ptr ||
-      !lse || !dn || !db)
-    return abi_error(SSA_ERR_NULL, "a tensor, lse, dn or db pointer is NULL");
+  if ((rc = abi_check_tensor(q, "q")) || (rc = abi_check_tensor(k, "k")) ||
+      (rc = abi_check_tensor(v, "v")) || (rc = abi_check_tensor(out, "out")) ||
+      (rc = abi_check_tensor(dout, "dout")) || (rc = abi_check_tensor(dq, "dq")) ||
+      (rc = abi_check_tensor(dk, "dk")) || (rc = abi_check_tensor(dv, "dv")))
+    return rc;
+  if (!lse || !dn || !db) return abi_error(SSA_ERR_NULL, "lse / dn / db is NULL");
   const Problem p = abi_to_problem(pr);
 
   // Scratch layout: delta [Hq x rows] fp32, then dn and db partials [B x Hq x tiles] fp32.

@@ -96,6 +96,27 @@ struct BwdArgs {
   int nkv;            // key blocks per sequence (ceil(max_seqlen / 128))
 };
 
+// dn / db partials of key block kvb for the GQA group of kv-head hkv: zero for a block past the
+// sequence end (nothing to add), NaN for a block that skipped or abandoned its work after a device
+// timeout (its dK / dV rows are NaN as well). Called by every thread of the block.
+template <bool BF16>
+__device__ __forceinline__ void bwd_block_partials(const BwdArgs& a, int z, int hkv, int kvb,
+                                                   int seq_start, int n0, int L, bool failed) {
+  const Problem& p = a.p;
+  const float v = failed ? nan_f32() : 0.f;
+  for (int i = threadIdx.x; i < 8 * p.gqa; i += blockDim.x) {
+    const int g = i >> 3, sub = i & 7;
+    const int64_t pi = ((int64_t)z * p.Hq + hkv * p.gqa + g) * (8 * a.nkv) + 8 * kvb + sub;
+    a.dn_part[pi] = v;
+    a.db_part[pi] = v;
+  }
+  if (failed) {
+    const int n1 = min(n0 + 128, L);
+    nan_fill_rows16<BF16>(a.dk, p, z, hkv, seq_start, n0, n1, nullptr);
+    nan_fill_rows16<BF16>(a.dv, p, z, hkv, seq_start, n0, n1, nullptr);
+  }
+}
+
 enum BwdBar : int {
   BB_KV = 0,
   BB_QF = 1,    // 3 stages: Q/dO tile + lse/delta landed
@@ -208,13 +229,10 @@ __global__ void __launch_bounds__(512, 1)
   int seq_start, L;
   seq_bounds(p, z, seq_start, L);
   const int n0 = kvb * C::BN;
+  // Block-uniform exits: a block past the sequence end has nothing to add; after a device
+  // timeout recorded by an earlier launch, this block's outputs are NaN.
   if (n0 >= L || *reinterpret_cast<volatile unsigned int*>(a.status) != 0) {
-    if (threadIdx.x < 8 * p.gqa) {  // keep the dn/db partials of an empty block well defined
-      const int g = threadIdx.x >> 3, sub = threadIdx.x & 7;
-      const int64_t pi = ((int64_t)z * p.Hq + hkv * p.gqa + g) * (8 * a.nkv) + 8 * kvb + sub;
-      a.dn_part[pi] = 0.f;
-      a.db_part[pi] = 0.f;
-    }
+    bwd_block_partials<BF16>(a, z, hkv, kvb, seq_start, n0, L, n0 < L);
     return;
   }
   const int q_start = p.causal ? n0 : 0;
@@ -638,6 +656,9 @@ __global__ void __launch_bounds__(512, 1)
     tc_fence_after();
     tmem_dealloc(tmem, C::TMEM_COLS);
   }
+  // A wait of this CTA expired: its dK / dV rows and dn / db partials are NaN, never partial
+  // results (dq is filled with NaN by the conversion kernel, which reads the status word).
+  if (*abort_flag) bwd_block_partials<BF16>(a, z, hkv, kvb, seq_start, n0, L, true);
 }
 
 // Backward preprocess for the tensor-core path, one pass: delta = rowsum(O * dO) in fp32
@@ -701,6 +722,7 @@ struct DndbArgs {
   int rows;  // leading grid rows that reduce
   float* dn;
   float* db;
+  const unsigned int* status;  // device status word: non-zero after an expired bounded wait
 };
 
 template <typename T, int D>
@@ -708,13 +730,18 @@ __global__ void __launch_bounds__(256) dq_convert_kernel(Problem p, const float*
                                                          int64_t dq_rows, TensorRef dq,
                                                          DndbArgs r) {
   griddep_wait();  // launched programmatically behind the backward kernel
+  // After a device timeout (this backward's or an earlier launch's) dq, dn and db are NaN.
+  const bool failed = *reinterpret_cast<const volatile unsigned int*>(r.status) != 0;
   if ((int)blockIdx.y < r.rows) {
     __shared__ double red[256];
     const int nred = (p.n_per_head ? p.Hq : 1) + 1;
     const int h = (int)blockIdx.y * (int)gridDim.x + (int)blockIdx.x;
-    if (h < nred)  // uniform per block
+    if (h < nred && failed) {
+      if (threadIdx.x == 0) (h < nred - 1 ? r.dn[h] : r.db[0]) = nan_f32();
+    } else if (h < nred) {  // uniform per block
       dndb_reduce_block<256>(h, r.dn_part, r.db_part, p.B, p.Hq, r.P, p.n_per_head, r.dn, r.db,
                              red);
+    }
     return;
   }
   constexpr int TPR = D / 8, RPB = 256 / TPR;
@@ -731,6 +758,11 @@ __global__ void __launch_bounds__(256) dq_convert_kernel(Problem p, const float*
   const float4 a0 = s[0], a1 = s[1];
   T* d = reinterpret_cast<T*>(dq.ptr) + row_offset(dq, p, z, hq, seq_start, row) + d0;
   uint4 w;
+  if (failed) {
+    const uint32_t nn = std::is_same<T, __nv_bfloat16>::value ? kNaNBf16x2 : kNaNF16x2;
+    *reinterpret_cast<uint4*>(d) = make_uint4(nn, nn, nn, nn);
+    return;
+  }
   if constexpr (std::is_same<T, __nv_bfloat16>::value) {
     w = make_uint4(pack2<true>(a0.x, a0.y), pack2<true>(a0.z, a0.w), pack2<true>(a1.x, a1.y),
                    pack2<true>(a1.z, a1.w));
@@ -770,7 +802,8 @@ int launch_dq_convert_dndb(const Problem& p, const float* dq_accum, int64_t dq_r
   const int extra_rows = (nred + gx - 1) / gx;
   dim3 gc((unsigned)gx, (unsigned)(p.B * p.Hq + extra_rows));
   if (launch_pdl(dq_convert_kernel<T, D>, gc, dim3(256), 0, st, p, dq_accum, dq_rows, dq,
-                 DndbArgs{dn_part, db_part, P, extra_rows, dn, db}) != cudaSuccess)
+                 DndbArgs{dn_part, db_part, P, extra_rows, dn, db, device_status_ptr()}) !=
+      cudaSuccess)
     return SSA_ERR_LAUNCH;
   note_launches(1);
   return SSA_OK;
@@ -863,13 +896,10 @@ __global__ void __launch_bounds__(512, 1)
   int seq_start, L;
   seq_bounds(p, z, seq_start, L);
   const int n0 = kvb * C::BN;
+  // Block-uniform exits: a block past the sequence end has nothing to add; after a device
+  // timeout recorded by an earlier launch, this block's outputs are NaN.
   if (n0 >= L || *reinterpret_cast<volatile unsigned int*>(a.status) != 0) {
-    if (threadIdx.x < 8 * p.gqa) {
-      const int g = threadIdx.x >> 3, sub = threadIdx.x & 7;
-      const int64_t pi = ((int64_t)z * p.Hq + hkv * p.gqa + g) * (8 * a.nkv) + 8 * kvb + sub;
-      a.dn_part[pi] = 0.f;
-      a.db_part[pi] = 0.f;
-    }
+    bwd_block_partials<BF16>(a, z, hkv, kvb, seq_start, n0, L, n0 < L);
     return;
   }
   const int q_start = p.causal ? n0 : 0;
@@ -1265,6 +1295,9 @@ __global__ void __launch_bounds__(512, 1)
     tc_fence_after();
     tmem_dealloc(tmem, C::TMEM_COLS);
   }
+  // A wait of this CTA expired: its dK / dV rows and dn / db partials are NaN, never partial
+  // results (dq is filled with NaN by the conversion kernel, which reads the status word).
+  if (*abort_flag) bwd_block_partials<BF16>(a, z, hkv, kvb, seq_start, n0, L, true);
 }
 
 struct BwdLayout {

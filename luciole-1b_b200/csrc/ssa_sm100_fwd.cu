@@ -112,8 +112,12 @@ __global__ void __launch_bounds__(192, 2)
   seq_bounds(p, z, seq_start, L);
   const int m0 = tile * C::BM;
   // Block-uniform exits, before any barrier or TMEM allocation: nothing to do, or an earlier
-  // launch already recorded a device-side timeout (later launches then cost nothing).
-  if (m0 >= L || *reinterpret_cast<volatile unsigned int*>(a.status) != 0) return;
+  // launch already recorded a device-side timeout (this tile's out and lse rows are then NaN).
+  if (m0 >= L) return;
+  if (*reinterpret_cast<volatile unsigned int*>(a.status) != 0) {
+    nan_fill_rows16<BF16>(a.o, p, z, hq, seq_start, m0, min(m0 + C::BM, L), a.lse);
+    return;
+  }
   const int kv_len = p.causal ? min(L, m0 + C::BM) : L;
   const int nblk = (kv_len + C::BN - 1) / C::BN;
   const int zc = p.cu_seqlens ? 0 : z;
@@ -428,6 +432,8 @@ __global__ void __launch_bounds__(192, 2)
     tc_fence_after();
     tmem_dealloc(tmem, C::TMEM_COLS);
   }
+  // A wait of this CTA expired: its tile's out / lse rows are NaN, never partial results.
+  if (*abort_flag) nan_fill_rows16<BF16>(a.o, p, z, hq, seq_start, m0, min(m0 + C::BM, L), a.lse);
 }
 
 template <int D, bool BF16>

@@ -184,6 +184,81 @@ def ssa_pair_backward_with_lse(q, k, v, out, dout, lse2, softmax_scale: float, s
     return dq, dk, dv, dn, db
 
 
+def ssa_reference_grads_blocked(q, k, v, softmax_scale: float, ssa_n, ssa_b, dout, causal: bool,
+                                heads=None, block: int = 512,
+                                compute_dtype=torch.float64) -> dict:
+    """The oracle of :func:`ssa_reference_grads` for long sequences, evaluated block by block so
+    that no [N, N] tensor is held (one [block, N] slab at a time).
+
+    Pass 1, per block of query rows, the rows of the eager forward (parity.py:169-206):
+    w = exp(n sign(s) log1p(b|s|)) over the visible keys, l = sum_j w, out = (w / l) V,
+    lse2 = log2 l. Pass 2, per block, the reference backward's per-element gradient math given
+    the final out and l (ssa_triton_kernel.py:348-397 for dK/dV/dn/db, :444-477 for dQ):
+        P = w / l,  delta = rowsum(out dout),  ds_ssa = P (dout V^T - delta),
+        ds = ds_ssa n b / (1 + b|s|),  dQ = ds K scale,  dK += ds^T Q scale,  dV += P^T dout,
+        dn += sum ds_ssa sign(s) log1p(b|s|),  db += sum ds_ssa n s / (1 + b|s|),
+    which is what autograd of the eager forward computes (pinned against it in the CPU tests).
+
+    q/dout [B, Hq, N, D], k/v [B, Hkv, N, D]. ``heads``: the q-heads to evaluate (default all);
+    rows of other heads stay zero in out/dq and contribute nothing to dk/dv/dn/db. Returns
+    dict(out, lse2, dq, dk, dv, dn, db) like :func:`ssa_reference_grads` (dn has ssa_n's shape).
+    """
+    cd = compute_dtype
+    bsz, hq, n_q, d = q.shape
+    hkv, n_k = k.shape[1], k.shape[2]
+    if hq % hkv != 0:
+        raise ValueError(f"HQ={hq} must be divisible by HKV={hkv}")
+    g = hq // hkv
+    heads = list(range(hq)) if heads is None else [int(h) for h in heads]
+    n_t = torch.as_tensor(ssa_n).detach().to(cd)
+    per_head = n_t.dim() == 1 and n_t.numel() == hq
+    b_val = float(torch.as_tensor(ssa_b))
+    scale = float(softmax_scale)
+    out = torch.zeros((bsz, hq, n_q, d), dtype=cd)
+    lse2 = torch.zeros((bsz, hq, n_q), dtype=cd)
+    dq = torch.zeros((bsz, hq, n_q, d), dtype=cd)
+    dk = torch.zeros((bsz, hkv, n_k, d), dtype=cd)
+    dv = torch.zeros((bsz, hkv, n_k, d), dtype=cd)
+    dn = torch.zeros(n_t.shape, dtype=cd)
+    db = torch.zeros((), dtype=cd)
+    for z in range(bsz):
+        for h in heads:
+            hk = h // g
+            nval = float(n_t.reshape(-1)[h if per_head else 0])
+            kf, vf = k[z, hk].to(cd), v[z, hk].to(cd)
+            qf, dof = q[z, h].to(cd), dout[z, h].to(cd)
+            dn_h = torch.zeros((), dtype=cd)
+            for m0 in range(0, n_q, block):
+                m1 = min(n_q, m0 + block)
+                nk = min(n_k, m1) if causal else n_k
+                s = (qf[m0:m1] @ kf[:nk].T) * scale
+                lg = torch.log1p(b_val * s.abs())
+                w = torch.exp(nval * torch.sign(s) * lg)
+                if causal:
+                    rows = torch.arange(m0, m1).unsqueeze(1)
+                    w = torch.where(torch.arange(nk).unsqueeze(0) <= rows, w, torch.zeros_like(w))
+                l = w.sum(-1, keepdim=True)
+                p = w / l.clamp_min(1e-12)
+                o = p @ vf[:nk]
+                out[z, h, m0:m1] = o
+                lse2[z, h, m0:m1] = torch.log2(l.clamp_min(1e-300)).squeeze(-1)
+                delta = (o * dof[m0:m1]).sum(-1, keepdim=True)
+                ds_ssa = p * (dof[m0:m1] @ vf[:nk].T - delta)
+                inv = 1.0 / (1.0 + b_val * s.abs())
+                ds = ds_ssa * (nval * b_val) * inv
+                dq[z, h, m0:m1] = (ds @ kf[:nk]) * scale
+                dk[z, hk, :nk] += (ds.T @ qf[m0:m1]) * scale
+                dv[z, hk, :nk] += p.T @ dof[m0:m1]
+                dn_h += (ds_ssa * torch.sign(s) * lg).sum()
+                db += (ds_ssa * (nval * s) * inv).sum()
+                del s, lg, w, p, ds_ssa, inv, ds
+            if per_head:
+                dn.view(-1)[h] += dn_h
+            else:
+                dn += dn_h
+    return {"out": out, "lse2": lse2, "dq": dq, "dk": dk, "dv": dv, "dn": dn, "db": db}
+
+
 def causal_score_elements(B: int, Hq: int, N: int, causal: bool) -> int:
     """Number of score elements E in the FlashAttention FLOP convention (S^2/2 causal)."""
     return B * Hq * (N * N // 2 if causal else N * N)
@@ -224,6 +299,7 @@ def max_rel(got, ref) -> float:
 
 __all__ = [
     "LOG2E", "ssa_reference_forward", "ssa_reference_grads", "ssa_reference_grads_varlen",
+    "ssa_reference_grads_blocked",
     "causal_score_elements", "attn_flops_fwd_bwd", "check_close", "max_rel",
 ]
 

@@ -28,7 +28,7 @@ def test_flop_counts_match_the_workloads(bench):
     bench.select_config("c4")  # B=1, Hq=32, S=32768, D=128
     assert bench.flops_per_rank() == pytest.approx(3.079e13, rel=1e-3)
     # special-function floor: lg2 + ex2 per element in each direction at 16 per clock per SM
-    sf = bench.sfu_floor(1.0)
+    sf = bench.sfu_floor(1.0, bench.score_elements())
     assert sf["ops_per_step"] == 4 * bench.score_elements()
     assert sf["floor_ms"] == pytest.approx(sf["ops_per_step"] / sf["peak_ops_per_s"] * 1e3)
     assert sf["frac"] == pytest.approx(sf["floor_ms"])
@@ -36,6 +36,46 @@ def test_flop_counts_match_the_workloads(bench):
     lens = bench.DOC_LENS
     assert sum(lens) == 65536 and all(1 <= L <= 4096 for L in lens)
     assert bench.score_elements() == 32 * sum(L * L // 2 for L in lens)
+
+
+def test_strong_scaling_shards_are_unit_rectangles(bench):
+    """Strong scaling splits the config's fixed batch by (batch, kv-head) units (SSA.shard's
+    balanced contiguous ranges): whole sequences when the ranks divide B, else kv-head ranges of
+    one sequence; every unit is owned exactly once."""
+    bench.select_config("c2")  # B = 8, Hkv = 8
+    for world in (1, 2, 4, 8, 16, 32, 64):
+        seen = set()
+        for rank in range(world):
+            bs, hs = bench.strong_shard(world, rank)
+            units = {(b, h) for b in range(bs.start, bs.stop) for h in range(hs.start, hs.stop)}
+            assert not units & seen
+            seen |= units
+            if world <= 8:
+                assert hs == slice(0, 8) and bs.stop - bs.start == 8 // world
+        assert seen == {(b, h) for b in range(8) for h in range(8)}
+    with pytest.raises(SystemExit):
+        bench.strong_shard(3, 0)
+    bench.select_config("c3")  # one packed sequence: kv-head ranges
+    assert [bench.strong_shard(2, r) for r in range(2)] == [(slice(0, 1), slice(0, 4)),
+                                                          (slice(0, 1), slice(4, 8))]
+    assert bench.shard_score_elements(1, 16) * 2 == bench.score_elements()
+
+
+def test_roofline_traffic_only_for_the_captured_source(bench, tmp_path, monkeypatch):
+    """roofline.traffic comes from the committed ncu summary only while the kernel source still
+    has the sha256 that capture recorded; otherwise it is null with a note."""
+    import hashlib
+    src = tmp_path / "k.cu"
+    src.write_text("kernel v1")
+    sha = hashlib.sha256(b"kernel v1").hexdigest()[:16]
+    prof = tmp_path / "p.md"
+    prof.write_text(f"bench-traffic: kernel=bwd sha256_16={sha} dram_bytes=1.5e9 workload=c2\n")
+    monkeypatch.setattr(bench, "TRAFFIC_PROFILE", prof)
+    monkeypatch.setattr(bench, "TRAFFIC_SOURCE", src)
+    assert bench.ncu_traffic()[0] == 1.5e9
+    src.write_text("kernel v2")
+    t, note = bench.ncu_traffic()
+    assert t is None and "stale" in note
 
 
 def test_reference_arm_prints_one_contract_line():
@@ -54,3 +94,4 @@ def test_reference_arm_prints_one_contract_line():
     assert d["cpu_baseline"]["kind"] in ("port", "reference") and d["cpu_baseline"]["cores"] >= 1
     assert d["e2e"]["value"] == d["value"]
     assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["e2e"]["d2h_bytes_per_step"] == 0
+    assert d["ms_per_step"] > 0 and d["sample_flops_per_step"] > 0

@@ -9,7 +9,8 @@ import torch
 
 from conftest import golden_qkv, load_golden
 from oracle.ssa_oracle import (attn_flops_fwd_bwd, causal_score_elements, max_rel,
-                               ssa_reference_grads, ssa_reference_grads_varlen)
+                               ssa_reference_grads, ssa_reference_grads_blocked,
+                               ssa_reference_grads_varlen)
 
 CASES = load_golden()
 
@@ -91,3 +92,41 @@ def test_flop_convention():
     # E = 8*32*2048^2/2 = 5.369e8, FLOPs = 14*64*E = 4.810e11
     assert causal_score_elements(8, 32, 2048, True) == 536870912
     assert math.isclose(attn_flops_fwd_bwd(8, 32, 2048, 64, True), 4.810e11, rel_tol=1e-3)
+
+
+@pytest.mark.parametrize("B,Hq,Hkv,N,D,causal,per_head,block", [
+    (2, 4, 2, 200, 32, True, True, 64),     # GQA, ragged last block
+    (1, 6, 3, 130, 16, False, False, 50),   # non-causal, scalar n
+    (1, 2, 1, 97, 64, True, False, 512),    # one block wider than the sequence
+])
+def test_blocked_oracle_matches_autograd_oracle(B, Hq, Hkv, N, D, causal, per_head, block):
+    """The blocked oracle used by the full-size GPU tests gives the autograd oracle's results."""
+    g = torch.Generator().manual_seed(B * 100 + N)
+    q = torch.randn(B, Hq, N, D, generator=g) * 0.5
+    k = torch.randn(B, Hkv, N, D, generator=g) * 0.5
+    v = torch.randn(B, Hkv, N, D, generator=g) * 0.5
+    do = torch.randn(B, Hq, N, D, generator=g)
+    n = 0.3 + 0.3 * torch.rand(Hq, generator=g) if per_head else torch.tensor(0.7)
+    b = torch.tensor(0.8)
+    r = ssa_reference_grads(q, k, v, D ** -0.5, n, b, do, causal)
+    rb = ssa_reference_grads_blocked(q, k, v, D ** -0.5, n, b, do, causal, block=block)
+    for name in r:
+        assert rb[name].shape == r[name].shape, name
+        assert (rb[name] - r[name]).abs().max() <= 1e-12 * (1 + r[name].abs().max()), name
+
+
+def test_blocked_oracle_head_subset():
+    """Evaluating a subset of q-heads gives those heads' rows and their share of dk/dv/dn/db."""
+    g = torch.Generator().manual_seed(5)
+    B, Hq, Hkv, N, D = 1, 4, 2, 96, 16
+    q, do = torch.randn(B, Hq, N, D, generator=g), torch.randn(B, Hq, N, D, generator=g)
+    k, v = torch.randn(B, Hkv, N, D, generator=g), torch.randn(B, Hkv, N, D, generator=g)
+    n, b = 0.3 + 0.3 * torch.rand(Hq, generator=g), torch.tensor(0.8)
+    do_sparse = torch.zeros_like(do)
+    do_sparse[:, 2] = do[:, 2]
+    full = ssa_reference_grads(q, k, v, 0.25, n, b, do_sparse, True)
+    sub = ssa_reference_grads_blocked(q, k, v, 0.25, n, b, do_sparse, True, heads=[2], block=32)
+    for name in ("out", "dq"):
+        assert torch.allclose(sub[name][:, 2], full[name][:, 2], atol=1e-12), name
+    for name in ("dk", "dv", "dn", "db"):
+        assert torch.allclose(sub[name], full[name], atol=1e-12), name

@@ -94,26 +94,91 @@ struct BwdArgs {
   float* db_part;
   unsigned int* status;
   int nkv;            // key blocks per sequence (ceil(max_seqlen / 128))
+  // q-head slices per key block: 1, or a divisor of the GQA ratio when the grid would leave SMs
+  // idle (few sequences). A slice's CTA holds partial dK / dV, written in fp32 to dkv_part
+  // [B][Hkv][nkv][hsplit][dK, dV][128 rows][D] and summed in slice order by the dq conversion.
+  int hsplit;
+  float* dkv_part;
 };
 
-// dn / db partials of key block kvb for the GQA group of kv-head hkv: zero for a block past the
-// sequence end (nothing to add), NaN for a block that skipped or abandoned its work after a device
-// timeout (its dK / dV rows are NaN as well). Called by every thread of the block.
+// CTA -> work unit. Key block 0 (the most query tiles) first, then the q-head slice, then the
+// (sequence, kv-head); a slice covers q-heads [g0, g0 + gh) of the GQA group.
+struct BwdUnit {
+  int kvb, sp, z, hkv, g0, gh;
+};
+__device__ __forceinline__ BwdUnit bwd_unit(const Problem& p, int hsplit) {
+  const int BHkv = p.B * p.Hkv;
+  const int per_kvb = BHkv * hsplit;
+  BwdUnit u;
+  u.kvb = (int)(blockIdx.x / per_kvb);
+  const int rem = (int)(blockIdx.x % per_kvb);
+  u.sp = rem / BHkv;
+  const int bh = rem % BHkv;
+  u.z = bh / p.Hkv;
+  u.hkv = bh % p.Hkv;
+  u.gh = p.gqa / hsplit;
+  u.g0 = u.sp * u.gh;
+  return u;
+}
+
+// Epilogue of one key row r (global row j) of dK (h = 0) or dV (h = 1): D fp32 accumulator columns
+// from TMEM at tcol, written in the output dtype, or in fp32 to the slice's partial rows.
+template <bool BF16, int D>
+__device__ __forceinline__ void store_dkv_row(const BwdArgs& a, const BwdUnit& u, int seq_start,
+                                              int h, int r, int j, int L, uint32_t tcol) {
+  using Tout = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
+  const Problem& p = a.p;
+  const TensorRef& dst = h ? a.dv : a.dk;
+  Tout* rowp = reinterpret_cast<Tout*>(dst.ptr) + row_offset(dst, p, u.z, u.hkv, seq_start, j);
+  float* prow = a.dkv_part +
+                (((((int64_t)u.z * p.Hkv + u.hkv) * a.nkv + u.kvb) * a.hsplit + u.sp) * 2 + h) *
+                    (128 * D) + (int64_t)r * D;
+#pragma unroll
+  for (int c = 0; c < D / 32; ++c) {
+    uint32_t o[32];
+    tmem_ld32(tcol + c * 32, o);
+    tmem_ld_wait(o);
+    if (j < L) {
+      if (a.hsplit > 1) {
+        float4* d4 = reinterpret_cast<float4*>(prow + c * 32);
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          d4[i] = make_float4(__uint_as_float(o[4 * i]), __uint_as_float(o[4 * i + 1]),
+                              __uint_as_float(o[4 * i + 2]), __uint_as_float(o[4 * i + 3]));
+      } else {
+        uint32_t w[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i)
+          w[i] = pack2<BF16>(__uint_as_float(o[2 * i]), __uint_as_float(o[2 * i + 1]));
+        uint4* d4 = reinterpret_cast<uint4*>(rowp + c * 32);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          d4[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
+      }
+    }
+  }
+}
+
+// dn / db partials of the unit's key block and q-head slice: zero for a block past the sequence
+// end (nothing to add), NaN for a block that skipped or abandoned its work after a device timeout
+// (its dK / dV rows are NaN as well; with q-head slices the dq conversion, which reads the status
+// word, writes them). Called by every thread of the block.
 template <bool BF16>
-__device__ __forceinline__ void bwd_block_partials(const BwdArgs& a, int z, int hkv, int kvb,
+__device__ __forceinline__ void bwd_block_partials(const BwdArgs& a, const BwdUnit& u,
                                                    int seq_start, int n0, int L, bool failed) {
   const Problem& p = a.p;
   const float v = failed ? nan_f32() : 0.f;
-  for (int i = threadIdx.x; i < 8 * p.gqa; i += blockDim.x) {
-    const int g = i >> 3, sub = i & 7;
-    const int64_t pi = ((int64_t)z * p.Hq + hkv * p.gqa + g) * (8 * a.nkv) + 8 * kvb + sub;
+  for (int i = threadIdx.x; i < 8 * u.gh; i += blockDim.x) {
+    const int g = u.g0 + (i >> 3), sub = i & 7;
+    const int64_t pi =
+        ((int64_t)u.z * p.Hq + u.hkv * p.gqa + g) * (8 * a.nkv) + 8 * u.kvb + sub;
     a.dn_part[pi] = v;
     a.db_part[pi] = v;
   }
-  if (failed) {
+  if (failed && a.hsplit == 1) {
     const int n1 = min(n0 + 128, L);
-    nan_fill_rows16<BF16>(a.dk, p, z, hkv, seq_start, n0, n1, nullptr);
-    nan_fill_rows16<BF16>(a.dv, p, z, hkv, seq_start, n0, n1, nullptr);
+    nan_fill_rows16<BF16>(a.dk, p, u.z, u.hkv, seq_start, n0, n1, nullptr);
+    nan_fill_rows16<BF16>(a.dv, p, u.z, u.hkv, seq_start, n0, n1, nullptr);
   }
 }
 
@@ -222,22 +287,21 @@ __global__ void __launch_bounds__(512, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const Problem& p = a.p;
-  const int BHkv = p.B * p.Hkv;
-  const int kvb = (int)(blockIdx.x / BHkv);  // key block 0 (most query tiles) first
-  const int bh = blockIdx.x % BHkv;
-  const int z = bh / p.Hkv, hkv = bh % p.Hkv;
+  const BwdUnit unit = bwd_unit(p, a.hsplit);  // key block 0 (most query tiles) first
+  const int kvb = unit.kvb, z = unit.z, hkv = unit.hkv;
+  const int hq0 = hkv * p.gqa + unit.g0;  // first q-head of this CTA's slice
   int seq_start, L;
   seq_bounds(p, z, seq_start, L);
   const int n0 = kvb * C::BN;
   // Block-uniform exits: a block past the sequence end has nothing to add; after a device
   // timeout recorded by an earlier launch, this block's outputs are NaN.
   if (n0 >= L || *reinterpret_cast<volatile unsigned int*>(a.status) != 0) {
-    bwd_block_partials<BF16>(a, z, hkv, kvb, seq_start, n0, L, n0 < L);
+    bwd_block_partials<BF16>(a, unit, seq_start, n0, L, n0 < L);
     return;
   }
   const int q_start = p.causal ? n0 : 0;
   const int T_h = (L - q_start + C::BT - 1) / C::BT;  // query tiles per q-head
-  const int T = T_h * p.gqa;
+  const int T = T_h * unit.gh;
   const int zc = p.cu_seqlens ? 0 : z;
 
   if (threadIdx.x == 0) {
@@ -285,7 +349,7 @@ __global__ void __launch_bounds__(512, 1)
     float pl[C::BT / 32], pd[C::BT / 32];
     auto fetch_stats = [&](int t) {
       const int g = t / T_h, tt = t - g * T_h;
-      const int hq = hkv * p.gqa + g;
+      const int hq = hq0 + g;
       const int m0 = q_start + tt * C::BT;
 #pragma unroll
       for (int k = 0; k < C::BT / 32; ++k) {
@@ -306,7 +370,7 @@ __global__ void __launch_bounds__(512, 1)
     for (int t = 0; t < T; ++t) {
       const int st = t % C::STAGES, u = t / C::STAGES;
       const int g = t / T_h, tt = t - g * T_h;
-      const int hq = hkv * p.gqa + g;
+      const int hq = hq0 + g;
       const int m0 = q_start + tt * C::BT;
       bool ok = true;
       if (t >= C::STAGES) ok = mbar_wait(bar(BB_QE + st), (u - 1) & 1, a.status);
@@ -467,7 +531,7 @@ __global__ void __launch_bounds__(512, 1)
     int st = 0, g = 0, tt = 0;  // ring stage, q-head within the group, tile within the head
     for (int t = 0; ok && t < T; ++t) {
       const int dsb = t & 1;
-      const int hq = hkv * p.gqa + g;
+      const int hq = hq0 + g;
       if (tt == 0) {
         n = load_n(p, hq);
         nbs = n * bval * p.scale;
@@ -571,24 +635,8 @@ __global__ void __launch_bounds__(512, 1)
     okd = __all_sync(0xffffffffu, okd);
     if (okd && !*abort_flag) {
       tc_fence_after();
-      using Tout = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
-      const TensorRef& dst = h ? a.dv : a.dk;
-      Tout* rowp = reinterpret_cast<Tout*>(dst.ptr) + row_offset(dst, p, z, hkv, seq_start, j);
-#pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        uint32_t o[32];
-        tmem_ld32(tmem + lane_off + (h ? C::COL_DV : C::COL_DK) + c * 32, o);
-        tmem_ld_wait(o);
-        if (j < L) {
-          uint32_t w[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i)
-            w[i] = pack2<BF16>(__uint_as_float(o[2 * i]), __uint_as_float(o[2 * i + 1]));
-          uint4* d4 = reinterpret_cast<uint4*>(rowp + c * 32);
-#pragma unroll
-          for (int i = 0; i < 4; ++i) d4[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
-        }
-      }
+      store_dkv_row<BF16, C::D>(a, unit, seq_start, h, r, j, L,
+                                tmem + lane_off + (h ? C::COL_DV : C::COL_DK));
     }
   } else {
     // ---------------------------------------------------------------- dQ drain (warps 8..11)
@@ -621,7 +669,7 @@ __global__ void __launch_bounds__(512, 1)
       tc_fence_before();
       mbar_arrive(bar(BB_SM));  // dQ(t) is out of TMEM: counts toward SM(t + 1)
       const int g = t / T_h, tt = t - g * T_h;
-      const int hq = hkv * p.gqa + g;
+      const int hq = hq0 + g;
       const int m0 = q_start + tt * C::BT + quad * 32;
       const int row0 = p.cu_seqlens ? (int)((int64_t)hq * a.dq_rows + seq_start + m0)
                                     : (int)(((int64_t)z * p.Hq + hq) * a.dq_rows + m0);
@@ -658,7 +706,7 @@ __global__ void __launch_bounds__(512, 1)
   }
   // A wait of this CTA expired: its dK / dV rows and dn / db partials are NaN, never partial
   // results (dq is filled with NaN by the conversion kernel, which reads the status word).
-  if (*abort_flag) bwd_block_partials<BF16>(a, z, hkv, kvb, seq_start, n0, L, true);
+  if (*abort_flag) bwd_block_partials<BF16>(a, unit, seq_start, n0, L, true);
 }
 
 // Backward preprocess for the tensor-core path, one pass: delta = rowsum(O * dO) in fp32
@@ -723,6 +771,11 @@ struct DndbArgs {
   float* dn;
   float* db;
   const unsigned int* status;  // device status word: non-zero after an expired bounded wait
+  // dK / dV from q-head slice partials (hsplit > 1): grid rows after the dq rows, one per
+  // (sequence, kv-head, dK or dV); fp32 [B][Hkv][nkv][hsplit][2][128][D] summed in slice order.
+  const float* dkv_part;
+  int hsplit, nkv;
+  TensorRef dk, dv;
 };
 
 template <typename T, int D>
@@ -746,6 +799,38 @@ __global__ void __launch_bounds__(256) dq_convert_kernel(Problem p, const float*
   }
   constexpr int TPR = D / 8, RPB = 256 / TPR;
   const int zh = (int)blockIdx.y - r.rows;
+  if (zh >= p.B * p.Hq) {  // dK / dV rows: sum the q-head slices' partials in order
+    const int u = zh - p.B * p.Hq;
+    const int z = u / (2 * p.Hkv), hkv = (u / 2) % p.Hkv, h = u & 1;
+    int seq_start, L;
+    seq_bounds(p, z, seq_start, L);
+    const int row = blockIdx.x * RPB + threadIdx.x / TPR;
+    const int d0 = (threadIdx.x % TPR) * 8;
+    if (row >= L) return;
+    const TensorRef& dst = h ? r.dv : r.dk;
+    T* d = reinterpret_cast<T*>(dst.ptr) + row_offset(dst, p, z, hkv, seq_start, row) + d0;
+    const uint32_t nn = std::is_same<T, __nv_bfloat16>::value ? kNaNBf16x2 : kNaNF16x2;
+    if (failed) {
+      *reinterpret_cast<uint4*>(d) = make_uint4(nn, nn, nn, nn);
+      return;
+    }
+    const int kvb = row >> 7;
+    const float* src = r.dkv_part +
+                       ((((int64_t)z * p.Hkv + hkv) * r.nkv + kvb) * r.hsplit * 2 + h) * (128 * D) +
+                       (int64_t)(row & 127) * D + d0;
+    float4 a0 = make_float4(0.f, 0.f, 0.f, 0.f), a1 = a0;
+    for (int sp = 0; sp < r.hsplit; ++sp) {
+      const float4* s4 = reinterpret_cast<const float4*>(src + (int64_t)sp * 2 * 128 * D);
+      const float4 b0 = s4[0], b1 = s4[1];
+      a0 = make_float4(a0.x + b0.x, a0.y + b0.y, a0.z + b0.z, a0.w + b0.w);
+      a1 = make_float4(a1.x + b1.x, a1.y + b1.y, a1.z + b1.z, a1.w + b1.w);
+    }
+    constexpr bool kBf = std::is_same<T, __nv_bfloat16>::value;
+    *reinterpret_cast<uint4*>(d) =
+        make_uint4(pack2<kBf>(a0.x, a0.y), pack2<kBf>(a0.z, a0.w), pack2<kBf>(a1.x, a1.y),
+                   pack2<kBf>(a1.z, a1.w));
+    return;
+  }
   const int z = zh / p.Hq, hq = zh % p.Hq;
   int seq_start, L;
   seq_bounds(p, z, seq_start, L);
@@ -795,15 +880,16 @@ cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t sme
 template <typename T, int D>
 int launch_dq_convert_dndb(const Problem& p, const float* dq_accum, int64_t dq_rows,
                             TensorRef dq, const float* dn_part, const float* db_part, int P,
-                            float* dn, float* db, cudaStream_t st) {
+                            float* dn, float* db, const BwdArgs& a, cudaStream_t st) {
   constexpr int RPB = 256 / (D / 8);
   const int gx = (p.max_seqlen + RPB - 1) / RPB;
   const int nred = (p.n_per_head ? p.Hq : 1) + 1;
   const int extra_rows = (nred + gx - 1) / gx;
-  dim3 gc((unsigned)gx, (unsigned)(p.B * p.Hq + extra_rows));
+  const int dkv_rows = a.hsplit > 1 ? p.B * p.Hkv * 2 : 0;
+  dim3 gc((unsigned)gx, (unsigned)(p.B * p.Hq + extra_rows + dkv_rows));
   if (launch_pdl(dq_convert_kernel<T, D>, gc, dim3(256), 0, st, p, dq_accum, dq_rows, dq,
-                 DndbArgs{dn_part, db_part, P, extra_rows, dn, db, device_status_ptr()}) !=
-      cudaSuccess)
+                 DndbArgs{dn_part, db_part, P, extra_rows, dn, db, device_status_ptr(),
+                          a.dkv_part, a.hsplit, a.nkv, a.dk, a.dv}) != cudaSuccess)
     return SSA_ERR_LAUNCH;
   note_launches(1);
   return SSA_OK;
@@ -889,31 +975,25 @@ __global__ void __launch_bounds__(512, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const Problem& p = a.p;
-  const int BHkv = p.B * p.Hkv;
-  const int kvb = (int)(blockIdx.x / BHkv);
-  const int bh = blockIdx.x % BHkv;
-  const int z = bh / p.Hkv, hkv = bh % p.Hkv;
+  const BwdUnit unit = bwd_unit(p, a.hsplit);
+  const int kvb = unit.kvb, z = unit.z, hkv = unit.hkv;
+  const int hq0 = hkv * p.gqa + unit.g0;
   int seq_start, L;
   seq_bounds(p, z, seq_start, L);
   const int n0 = kvb * C::BN;
   // Block-uniform exits: a block past the sequence end has nothing to add; after a device
   // timeout recorded by an earlier launch, this block's outputs are NaN.
   if (n0 >= L || *reinterpret_cast<volatile unsigned int*>(a.status) != 0) {
-    bwd_block_partials<BF16>(a, z, hkv, kvb, seq_start, n0, L, n0 < L);
+    bwd_block_partials<BF16>(a, unit, seq_start, n0, L, n0 < L);
     return;
   }
   const int q_start = p.causal ? n0 : 0;
   const int T_h = (L - q_start + C::BT - 1) / C::BT;
-  const int T = T_h * p.gqa;
+  const int T = T_h * unit.gh;
   const int zc = p.cu_seqlens ? 0 : z;
   // A P/dS group may own no tile of some q-head (tiles alternate between the groups): start
   // every partial of this block at zero; the __syncthreads below orders these writes first.
-  if (threadIdx.x < 8 * p.gqa) {
-    const int g = threadIdx.x >> 3, sub = threadIdx.x & 7;
-    const int64_t pi = ((int64_t)z * p.Hq + hkv * p.gqa + g) * (8 * a.nkv) + 8 * kvb + sub;
-    a.dn_part[pi] = 0.f;
-    a.db_part[pi] = 0.f;
-  }
+  bwd_block_partials<BF16>(a, unit, seq_start, n0, L, false);
 
   if (threadIdx.x == 0) {
     mbar_init(bar(B2_KV), 1);
@@ -967,7 +1047,7 @@ __global__ void __launch_bounds__(512, 1)
       float pl[2], pd[2];
       auto fetch_stats = [&](int t) {
         const int g = t / T_h, tt = t - g * T_h;
-        const int hq = hkv * p.gqa + g;
+        const int hq = hq0 + g;
         const int m0 = q_start + tt * C::BT;
 #pragma unroll
         for (int k2 = 0; k2 < 2; ++k2) {
@@ -985,7 +1065,7 @@ __global__ void __launch_bounds__(512, 1)
       for (int t = 0; t < T; ++t) {
         const int st = t % C::STAGES, u = t / C::STAGES;
         const int g = t / T_h, tt = t - g * T_h;
-        const int hq = hkv * p.gqa + g;
+        const int hq = hq0 + g;
         const int m0 = q_start + tt * C::BT;
         bool ok = true;
         if (t >= C::STAGES) ok = mbar_wait(bar(B2_QE + st), (u - 1) & 1, a.status);
@@ -1129,7 +1209,7 @@ __global__ void __launch_bounds__(512, 1)
     for (int t = h; t < T; t += 2) {
       const int st = t % C::STAGES;
       const int g = t / T_h, tt = t - g * T_h;
-      const int hq = hkv * p.gqa + g;
+      const int hq = hq0 + g;
       n = load_n(p, hq);
       nbs = n * bval * p.scale;
       const int mh = q_start + tt * C::BT;
@@ -1219,24 +1299,8 @@ __global__ void __launch_bounds__(512, 1)
     okd = __all_sync(0xffffffffu, okd);
     if (okd && !*abort_flag) {
       tc_fence_after();
-      using Tout = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
-      const TensorRef& dst = h ? a.dv : a.dk;
-      Tout* rowp = reinterpret_cast<Tout*>(dst.ptr) + row_offset(dst, p, z, hkv, seq_start, j);
-#pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t o[32];
-        tmem_ld32(tmem + lane_off + (h ? C::COL_DV : C::COL_DK) + c * 32, o);
-        tmem_ld_wait(o);
-        if (j < L) {
-          uint32_t w[16];
-#pragma unroll
-          for (int i = 0; i < 16; ++i)
-            w[i] = pack2<BF16>(__uint_as_float(o[2 * i]), __uint_as_float(o[2 * i + 1]));
-          uint4* d4 = reinterpret_cast<uint4*>(rowp + c * 32);
-#pragma unroll
-          for (int i = 0; i < 4; ++i) d4[i] = make_uint4(w[4 * i], w[4 * i + 1], w[4 * i + 2], w[4 * i + 3]);
-        }
-      }
+      store_dkv_row<BF16, C::D>(a, unit, seq_start, h, r, j, L,
+                                tmem + lane_off + (h ? C::COL_DV : C::COL_DK));
     }
   } else {
     // ------------------------------------------------------------ dQ^T drain (warps 8..11)
@@ -1274,7 +1338,7 @@ __global__ void __launch_bounds__(512, 1)
       __syncwarp();
       if (lane == 0) {
         const int g = t / T_h, tt = t - g * T_h;
-        const int hq = hkv * p.gqa + g;
+        const int hq = hq0 + g;
         const int m0 = q_start + tt * C::BT;
         const int row0 = p.cu_seqlens ? (int)((int64_t)hq * a.dq_rows + seq_start + m0)
                                       : (int)(((int64_t)z * p.Hq + hq) * a.dq_rows + m0);
@@ -1297,14 +1361,54 @@ __global__ void __launch_bounds__(512, 1)
   }
   // A wait of this CTA expired: its dK / dV rows and dn / db partials are NaN, never partial
   // results (dq is filled with NaN by the conversion kernel, which reads the status word).
-  if (*abort_flag) bwd_block_partials<BF16>(a, z, hkv, kvb, seq_start, n0, L, true);
+  if (*abort_flag) bwd_block_partials<BF16>(a, unit, seq_start, n0, L, true);
 }
 
 struct BwdLayout {
-  int nkv;
+  int nkv, hsplit;
   int64_t dq_rows;
-  size_t dq_bytes, part_bytes, total;
+  size_t dq_bytes, part_bytes, dkv_bytes, total;
 };
+
+constexpr int kNumSMs = 148;      // B200
+constexpr double kCtaCost = 4.0;  // per-CTA fixed cost of the backward, in query-tile periods
+
+// q-head slices per key block (see BwdArgs::hsplit): the divisor s of the GQA ratio that
+// minimises max(longest CTA, average work per SM), in query tiles of `bt` rows with a fixed cost
+// of four tiles per CTA (setup, first loads, pipeline fill and the dK / dV epilogue; this value
+// reproduces the measured B200 choices at config-2 shapes: B = 1 -> 2 slices, 0.203 -> 0.138 ms;
+// B = 2 -> 1, where 2 slices measured 0.218 against 0.198 ms). A dense estimate (every sequence
+// max_seqlen long); another s must be at least 3% better than the smaller one to be taken.
+// SSA_BWD_HSPLIT overrides it (a divisor of the GQA ratio) for measurements.
+int choose_hsplit(const Problem& p, int bt) {
+  if (const char* e = getenv("SSA_BWD_HSPLIT")) {
+    const int s = atoi(e);
+    if (s >= 1 && p.gqa % s == 0) return s;
+  }
+  const int nkv = (p.max_seqlen + 127) / 128;
+  const double units = (double)p.B * p.Hkv;
+  double total = 0.0, longest = 0.0;
+  for (int kvb = 0; kvb < nkv; ++kvb) {
+    const int rows = p.causal ? p.max_seqlen - 128 * kvb : p.max_seqlen;
+    const double th = (double)((rows + bt - 1) / bt);
+    total += th;
+    longest = longest > th ? longest : th;
+  }
+  total *= units * p.gqa;
+  int best = 1;
+  double best_cost = 1e300;
+  for (int s = 1; s <= p.gqa && s <= 8; ++s) {
+    if (p.gqa % s) continue;
+    const double ctas = nkv * units * s;
+    const double c1 = longest * p.gqa / s + kCtaCost, c2 = (total + kCtaCost * ctas) / kNumSMs;
+    const double cost = c1 > c2 ? c1 : c2;
+    if (cost < best_cost * 0.97) {
+      best = s;
+      best_cost = cost;
+    }
+  }
+  return best;
+}
 
 inline size_t al256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 
@@ -1321,7 +1425,11 @@ BwdLayout bwd_layout(const Problem& p) {
     l.dq_bytes = al256(sizeof(float) * (size_t)p.B * p.Hq * l.dq_rows * p.D);
   }
   l.part_bytes = al256(sizeof(float) * (size_t)p.B * p.Hq * 8 * l.nkv);
-  l.total = l.dq_bytes + 2 * l.part_bytes;
+  l.hsplit = choose_hsplit(p, p.D == 128 ? 64 : 128);
+  l.dkv_bytes = l.hsplit > 1 ? al256(sizeof(float) * (size_t)p.B * p.Hkv * l.nkv * l.hsplit * 2 *
+                                     128 * p.D)
+                             : 0;
+  l.total = l.dq_bytes + 2 * l.part_bytes + l.dkv_bytes;
   return l;
 }
 
@@ -1352,6 +1460,10 @@ int run_bwd(const Problem& p, TensorRef q, TensorRef k, TensorRef v, TensorRef o
   a.db_part = reinterpret_cast<float*>(w + lay.dq_bytes + lay.part_bytes);
   a.status = device_status_ptr();
   a.nkv = lay.nkv;
+  a.hsplit = lay.hsplit;
+  a.dkv_part = lay.hsplit > 1
+                   ? reinterpret_cast<float*>(w + lay.dq_bytes + 2 * lay.part_bytes)
+                   : nullptr;
   {
     using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
     dim3 gp((unsigned)((lay.dq_rows + 31) / 32), p.cu_seqlens ? p.Hq : p.B * p.Hq);
@@ -1378,14 +1490,14 @@ int run_bwd(const Problem& p, TensorRef q, TensorRef k, TensorRef v, TensorRef o
   auto kern = bwd_sm100_kernel<BF16>;
   if (set_smem_limit_once(reinterpret_cast<const void*>(kern), (int)C::SMEM_BYTES) != SSA_OK)
     return SSA_ERR_CUDA;
-  const long long grid = (long long)lay.nkv * p.B * p.Hkv;
+  const long long grid = (long long)lay.nkv * p.B * p.Hkv * lay.hsplit;
   if (launch_pdl(kern, dim3((unsigned)grid), dim3(C::THREADS), C::SMEM_BYTES, st, tq, tk, tv, tdo,
                  tdq, a) != cudaSuccess)
     return SSA_ERR_LAUNCH;
   note_launches(1);
   using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
   return launch_dq_convert_dndb<T, 64>(p, a.dq_accum, a.dq_rows, dq, a.dn_part, a.db_part,
-                                       8 * lay.nkv, dn, db, st);
+                                       8 * lay.nkv, dn, db, a, st);
 }
 
 template <bool BF16>
@@ -1416,6 +1528,10 @@ int run_bwd128(const Problem& p, TensorRef q, TensorRef k, TensorRef v, TensorRe
   a.db_part = reinterpret_cast<float*>(w + lay.dq_bytes + lay.part_bytes);
   a.status = device_status_ptr();
   a.nkv = lay.nkv;
+  a.hsplit = lay.hsplit;
+  a.dkv_part = lay.hsplit > 1
+                   ? reinterpret_cast<float*>(w + lay.dq_bytes + 2 * lay.part_bytes)
+                   : nullptr;
   {
     dim3 gp((unsigned)((lay.dq_rows + 15) / 16), p.cu_seqlens ? p.Hq : p.B * p.Hq);
     bwd_preprocess_sm100_kernel<T, 128><<<gp, 256, 0, st>>>(p, out, dout, delta, a.dq_accum,
@@ -1437,11 +1553,11 @@ int run_bwd128(const Problem& p, TensorRef q, TensorRef k, TensorRef v, TensorRe
   auto kern = bwd128_sm100_kernel<BF16>;
   if (set_smem_limit_once(reinterpret_cast<const void*>(kern), (int)C::SMEM_BYTES) != SSA_OK)
     return SSA_ERR_CUDA;
-  const long long grid = (long long)lay.nkv * p.B * p.Hkv;
+  const long long grid = (long long)lay.nkv * p.B * p.Hkv * lay.hsplit;
   kern<<<(unsigned)grid, C::THREADS, C::SMEM_BYTES, st>>>(tq, tk, tv, tdo, tdq, a);
   note_launches(2);
   return launch_dq_convert_dndb<T, 128>(p, a.dq_accum, a.dq_rows, dq, a.dn_part, a.db_part,
-                                        8 * lay.nkv, dn, db, st);
+                                        8 * lay.nkv, dn, db, a, st);
 }
 
 }  // namespace sm100

@@ -126,6 +126,40 @@ def test_kernel_vs_oracle(B, Hq, Hkv, N, D, causal, dtype, per_head, cuda_device
     assert_scalar_close("db", r["db"], ref["db"])
 
 
+@pytest.mark.parametrize("D", [64, 128])
+def test_qhead_slices_of_a_key_block(D, cuda_device, monkeypatch):
+    """With few sequences the backward splits each key block's GQA q-heads over 2 or 4 CTAs
+    (their fp32 dK / dV partials are summed in slice order by the dq conversion). Every split,
+    forced here through SSA_BWD_HSPLIT, matches the oracle, and dK / dV differ between splits by
+    rounding only."""
+    K = _api()
+    B, Hq, Hkv, N = 1, 8, 2, 700  # ragged last key block
+    q = seeded((B, Hq, N, D), 301, 0.5)
+    k = seeded((B, Hkv, N, D), 302, 0.5)
+    v = seeded((B, Hkv, N, D), 303, 0.5)
+    do = seeded((B, Hq, N, D), 304)
+    n = 0.3 + 0.3 * torch.rand(Hq, generator=torch.Generator().manual_seed(305))
+    b = torch.tensor(0.8)
+    scale = D ** -0.5
+    ref = ssa_reference_grads(q, k, v, scale, n, b, do, True)
+    dev = cuda_device
+    got = {}
+    for s in (1, 2, 4):
+        monkeypatch.setenv("SSA_BWD_HSPLIT", str(s))
+        r = run_fwd_bwd(q.to(dev), k.to(dev), v.to(dev), do.to(dev), scale, n.to(dev),
+                        b.to(dev), True)
+        for name in ("out", "dq", "dk", "dv"):
+            assert_lowp_close(f"{name} (slices {s})", r[name], ref[name])
+        assert_scalar_close(f"dn (slices {s})", r["dn"], ref["dn"])
+        assert_scalar_close(f"db (slices {s})", r["db"], ref["db"])
+        got[s] = r
+    for s in (2, 4):
+        for name in ("dk", "dv"):
+            d = (got[s][name].float() - got[1][name].float()).abs()
+            assert (d <= got[1][name].float().abs() * 2 ** -7 + 1e-6).all(), (s, name)
+        assert torch.equal(got[s]["out"], got[1]["out"])
+
+
 def test_strided_megatron_layout(cuda_device):
     """[S, B, H, D]-permuted views (check_ssa_triton_parity.py:262-265) go through TMA as-is."""
     K = _api()

@@ -70,6 +70,14 @@ typedef struct {
    * Document z then occupies rows [cu_seqlens_padded[z], + cu_seqlens[z+1] - cu_seqlens[z]);
    * rows between documents are not read and not written. NULL: documents are contiguous. */
   const int32_t* cu_seqlens_padded;
+  /* Backward only. 0: dq is accumulated across key blocks with fp32 reduce-adds in whatever order
+   * the blocks finish, so it may differ in the last bits from run to run (dk, dv, dn, db are
+   * always bit-reproducible). 1: the tensor-core backward adds every dQ tile's contributions in
+   * ascending key-block order (bounded waits between CTAs; a wait that expires records
+   * SSA_ERR_DEVICE_TIMEOUT), so dq is bit-identical from run to run, as the reference's
+   * determinism suite requires (check_ssa_triton_parity.py:507-562). The generic kernels are
+   * deterministic in both modes. Costs extra workspace and some speed. */
+  int32_t deterministic;
 } ssa_problem_t;
 
 /* Forward. Replaces ssa_flash_attn_forward (ssa_triton_kernel.py:732-792) and the

@@ -47,7 +47,14 @@ class SsaProblem(ctypes.Structure):
                 ("causal", ctypes.c_int32), ("softmax_scale", ctypes.c_float),
                 ("ssa_n", ctypes.c_void_p), ("n_per_head", ctypes.c_int32),
                 ("ssa_b", ctypes.c_void_p), ("cu_seqlens", ctypes.c_void_p),
-                ("max_seqlen", ctypes.c_int32), ("cu_seqlens_padded", ctypes.c_void_p)]
+                ("max_seqlen", ctypes.c_int32), ("cu_seqlens_padded", ctypes.c_void_p),
+                ("deterministic", ctypes.c_int32)]
+
+
+def deterministic_default() -> bool:
+    """The backward's dq accumulation mode when a call does not choose: SSA_DETERMINISTIC=1 in the
+    environment selects the ordered (bit-reproducible) accumulation."""
+    return os.environ.get("SSA_DETERMINISTIC", "0") not in ("", "0", "false", "False")
 
 
 class SSAKernelError(RuntimeError):

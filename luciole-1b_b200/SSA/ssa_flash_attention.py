@@ -35,13 +35,17 @@ class SSAFlashAttnFunc(Function):
     """out = softmax(n * sign(s) * log1p(b |s|)) @ V with s = scale * Q K^T (causal optional)."""
 
     @staticmethod
-    def forward(ctx, q, k, v, softmax_scale, ssa_n, ssa_b, causal, dropout_p, training):
+    def forward(ctx, q, k, v, softmax_scale, ssa_n, ssa_b, causal, dropout_p, training,
+                deterministic=None):
+        # deterministic (optional 10th argument, no reference counterpart): bit-reproducible dq
+        # in the backward; None takes SSA_DETERMINISTIC from the environment.
         ssa_n_f32 = ssa_n.float().contiguous()
         ssa_b_f32 = ssa_b.float().contiguous()
         out, m = ssa_flash_attn_forward(q, k, v, softmax_scale, ssa_n_f32, ssa_b_f32, causal)
         ctx.save_for_backward(q, k, v, out, m, ssa_n_f32, ssa_b_f32)
         ctx.softmax_scale = softmax_scale
         ctx.causal = causal
+        ctx.deterministic = deterministic
         ctx.dropout_p = dropout_p
         ctx.n_meta = (ssa_n.shape, ssa_n.dtype)
         ctx.b_meta = (ssa_b.shape, ssa_b.dtype)
@@ -54,18 +58,21 @@ class SSAFlashAttnFunc(Function):
         # strides, so a Megatron-layout gradient ([B, H, S, D] view of [S, B, H*D]) is read in
         # place and only layouts the kernels cannot address are copied (in the kernel wrapper).
         dq, dk, dv, dn, db = ssa_flash_attn_backward(
-            q, k, v, out, dout, m, ctx.softmax_scale, ssa_n_f32, ssa_b_f32, ctx.causal)
+            q, k, v, out, dout, m, ctx.softmax_scale, ssa_n_f32, ssa_b_f32, ctx.causal,
+            deterministic=ctx.deterministic)
         dn = dn.reshape(ctx.n_meta[0]).to(ctx.n_meta[1])
         db = db.reshape(ctx.b_meta[0]).to(ctx.b_meta[1])
-        return dq, dk, dv, None, dn, db, None, None, None
+        grads = (dq, dk, dv, None, dn, db, None, None, None, None)
+        return grads[:len(ctx.needs_input_grad)]  # 9 for the reference's 9 arguments
 
 
 def ssa_flash_attention(q, k, v, softmax_scale, ssa_n, ssa_b, causal=True, dropout_p=0.0,
-                        training=True):
+                        training=True, deterministic=None):
     """High-level API (reference ssa_flash_attention.py:69-97): q [B, Hq, N, D],
-    k/v [B, Hkv, N, D] (native GQA), ssa_n 0-d or [Hq], ssa_b 0-d. Returns [B, Hq, N, D]."""
+    k/v [B, Hkv, N, D] (native GQA), ssa_n 0-d or [Hq], ssa_b 0-d. Returns [B, Hq, N, D].
+    deterministic: bit-reproducible dq in the backward (default: SSA_DETERMINISTIC)."""
     return SSAFlashAttnFunc.apply(q, k, v, softmax_scale, ssa_n, ssa_b, causal, dropout_p,
-                                  training)
+                                  training, deterministic)
 
 
 class SSAVarlenFlashAttnFunc(Function):

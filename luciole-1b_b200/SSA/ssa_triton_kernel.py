@@ -50,7 +50,8 @@ def _params(ssa_n: torch.Tensor, ssa_b: torch.Tensor, hq: int, device) -> Tuple[
 def _problem(q: torch.Tensor, hkv: int, softmax_scale: float, n: torch.Tensor, b: torch.Tensor,
              per_head: int, causal: bool, B: int, N: int,
              cu_seqlens: Optional[torch.Tensor] = None, max_seqlen: int = 0,
-             cu_seqlens_padded: Optional[torch.Tensor] = None) -> _lib.SsaProblem:
+             cu_seqlens_padded: Optional[torch.Tensor] = None,
+             deterministic: bool = False) -> _lib.SsaProblem:
     if q.dtype not in _lib.DTYPE_CODES:
         raise ValueError(f"unsupported dtype {q.dtype}")
     hq, d = q.shape[1], q.shape[-1]
@@ -58,7 +59,8 @@ def _problem(q: torch.Tensor, hkv: int, softmax_scale: float, n: torch.Tensor, b
         _lib.DTYPE_CODES[q.dtype], B, hq, hkv, N, d, 1 if causal else 0, float(softmax_scale),
         n.data_ptr(), per_head, b.data_ptr(),
         cu_seqlens.data_ptr() if cu_seqlens is not None else None, int(max_seqlen),
-        cu_seqlens_padded.data_ptr() if cu_seqlens_padded is not None else None)
+        cu_seqlens_padded.data_ptr() if cu_seqlens_padded is not None else None,
+        1 if deterministic else 0)
 
 
 def _tma_ok(t: torch.Tensor) -> bool:
@@ -150,17 +152,24 @@ def _param_grad_pair(n, device):
     return buf[:k].view(n.shape), buf[k]
 
 
-def ssa_flash_attn_backward(q, k, v, out, dout, m, softmax_scale, ssa_n, ssa_b, causal=True):
+def ssa_flash_attn_backward(q, k, v, out, dout, m, softmax_scale, ssa_n, ssa_b, causal=True,
+                            deterministic=None):
     """Backward (reference ssa_triton_kernel.py:795-897).
 
     Returns (dq, dk, dv, dn, db): dq/dk/dv in the inputs' dtype and layout; dn fp32 with
     ssa_n's shape (0-d in the reference); db a 0-d fp32 tensor. dn/db are reduced on the
     device (fp64, deterministic); no host synchronisation happens.
+
+    deterministic: True adds each dQ tile's contributions in a fixed order, so dq is
+    bit-identical from run to run (the reference's determinism rule,
+    check_ssa_triton_parity.py:507-562); dk, dv, dn and db are bit-reproducible either way.
+    None (default) takes SSA_DETERMINISTIC from the environment (off unless set to 1).
     """
     lib = _lib.load()
     B, Hq, Hkv, N, D = _check_qkv(q, k, v)
     n, b, per_head = _params(ssa_n, ssa_b, Hq, q.device)
-    prob = _problem(q, Hkv, softmax_scale, n, b, per_head, causal, B, N)
+    det = _lib.deterministic_default() if deterministic is None else bool(deterministic)
+    prob = _problem(q, Hkv, softmax_scale, n, b, per_head, causal, B, N, deterministic=det)
     fam = lib.ssa_attn_kernel_family(ctypes.byref(prob))
     q, k, v, dout = _prep(q, fam), _prep(k, fam), _prep(v, fam), _prep(dout, fam)
     out = _prep(out, fam)
@@ -236,15 +245,17 @@ def ssa_flash_attn_varlen_forward(q, k, v, cu_seqlens, max_seqlen, softmax_scale
 
 def ssa_flash_attn_varlen_backward(q, k, v, out, dout, lse, cu_seqlens, max_seqlen,
                                    softmax_scale, ssa_n, ssa_b, causal=True,
-                                   cu_seqlens_padded=None):
+                                   cu_seqlens_padded=None, deterministic=None):
     """Backward of :func:`ssa_flash_attn_varlen_forward`. Returns (dq, dk, dv, dn, db); with
-    cu_seqlens_padded the gradient rows of padding tokens are zero."""
+    cu_seqlens_padded the gradient rows of padding tokens are zero. ``deterministic`` as in
+    :func:`ssa_flash_attn_backward`."""
     lib = _lib.load()
     T, Hq, Hkv, D, ndoc = _check_thd(q, k, v, cu_seqlens)
     cu_pad = _check_padded(cu_seqlens, cu_seqlens_padded)
     n, b, per_head = _params(ssa_n, ssa_b, Hq, q.device)
+    det = _lib.deterministic_default() if deterministic is None else bool(deterministic)
     prob = _problem(q, Hkv, softmax_scale, n, b, per_head, causal, ndoc, T,
-                    cu_seqlens, max_seqlen, cu_pad)
+                    cu_seqlens, max_seqlen, cu_pad, deterministic=det)
     fam = lib.ssa_attn_kernel_family(ctypes.byref(prob))
     q, k, v, dout = _prep(q, fam), _prep(k, fam), _prep(v, fam), _prep(dout, fam)
     out = _prep(out, fam)

@@ -83,6 +83,7 @@ Problem to_problem(const ssa_problem_t* pr) {
   p.cu_seqlens = pr->cu_seqlens;
   p.cu_seqlens_padded = pr->cu_seqlens ? pr->cu_seqlens_padded : nullptr;
   p.max_seqlen = pr->cu_seqlens ? pr->max_seqlen : pr->N;
+  p.det = pr->deterministic ? 1 : 0;
   return p;
 }
 

@@ -36,6 +36,7 @@ struct Problem {
   const int* cu_seqlens;         // nullptr: dense
   const int* cu_seqlens_padded;  // packed with padding: start row of each document, or nullptr
   int max_seqlen;                // rows a sequence can have (N when dense)
+  int det;                       // tensor-core backward: bit-reproducible dq (ordered dQ adds)
 };
 
 struct TensorRef {

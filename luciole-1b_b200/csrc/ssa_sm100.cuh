@@ -286,6 +286,37 @@ __device__ __forceinline__ void bulk_wait0() {
   asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
 }
 
+// ----------------------------------------------------------------------------- semaphores
+// Ordered accumulation across CTAs (deterministic dQ): a CTA waits until a global counter reaches
+// its turn, adds, waits for its adds to complete, then releases the next turn.
+// Waits until *sem == val (acquire, GPU scope); false after ~limit cycles, with the timeout
+// recorded in the device status word. The caller's later async-proxy (TMA) operations are
+// ordered after the acquire by a proxy fence.
+__device__ __forceinline__ bool sem_wait_eq(const int* sem, int val, unsigned int* status,
+                                            long long limit = kWaitCycles) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(sem) : "memory");
+  if (v != val) {
+    const long long t0 = clock64();
+    while (true) {
+      asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(sem) : "memory");
+      if (v == val) break;
+      if (clock64() - t0 > limit) {
+        atomicOr(status, 1u);
+        return false;
+      }
+    }
+  }
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+  return true;
+}
+// After this thread's bulk async groups have completed (bulk_wait0): makes their global writes
+// visible, then passes the turn on (*sem += 1, release, GPU scope).
+__device__ __forceinline__ void sem_release_next(int* sem) {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+  asm volatile("red.release.gpu.global.add.s32 [%0], 1;" ::"l"(sem) : "memory");
+}
+
 // Per-warpgroup register budget changes (all four warps of the warpgroup execute the same one).
 template <uint32_t N>
 __device__ __forceinline__ void regs_inc() {

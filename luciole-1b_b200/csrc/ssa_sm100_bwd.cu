@@ -99,7 +99,33 @@ struct BwdArgs {
   // [B][Hkv][nkv][hsplit][dK, dV][128 rows][D] and summed in slice order by the dq conversion.
   int hsplit;
   float* dkv_part;
+  // dn / db partials per (sequence, q-head, key block): 8 (two halves x four warps), or, with
+  // deterministic dq (tile-major order, heads alternating), 8 per query tile: ppk = 8 * ntq.
+  int ppk;
+  int ntq;      // query tiles per sequence (ceil(max_seqlen / query tile rows))
+  int* dq_sem;  // deterministic dq: turn counters [B][Hq][ntq][4 drain warps], zeroed per call
 };
+
+__device__ __forceinline__ int64_t bwd_partial_index(const BwdArgs& a, int z, int hq, int kvb,
+                                                     int tile_slot) {
+  return ((int64_t)z * a.p.Hq + hq) * ((int64_t)a.ppk * a.nkv) + (int64_t)a.ppk * kvb +
+         8 * tile_slot;
+}
+
+// Tile t of a CTA's loop -> (q-head g within its slice, query tile tt within the head). Default
+// order: heads outer, tiles ascending. Deterministic-dQ order: tiles descending outer, heads inner,
+// so the CTAs of all key blocks of a (sequence, slice) reach a query tile together and the
+// ordered dQ adds pass along the key blocks with a short lag that does not grow.
+__device__ __forceinline__ void tile_coords(int t, int T_h, int gh, int det, int& g, int& tt) {
+  if (det) {
+    const int k = t / gh;
+    g = t - k * gh;
+    tt = T_h - 1 - k;
+  } else {
+    g = t / T_h;
+    tt = t - g * T_h;
+  }
+}
 
 // CTA -> work unit. Key block 0 (the most query tiles) first, then the q-head slice, then the
 // (sequence, kv-head); a slice covers q-heads [g0, g0 + gh) of the GQA group.
@@ -168,10 +194,9 @@ __device__ __forceinline__ void bwd_block_partials(const BwdArgs& a, const BwdUn
                                                    int seq_start, int n0, int L, bool failed) {
   const Problem& p = a.p;
   const float v = failed ? nan_f32() : 0.f;
-  for (int i = threadIdx.x; i < 8 * u.gh; i += blockDim.x) {
-    const int g = u.g0 + (i >> 3), sub = i & 7;
-    const int64_t pi =
-        ((int64_t)u.z * p.Hq + u.hkv * p.gqa + g) * (8 * a.nkv) + 8 * u.kvb + sub;
+  for (int i = threadIdx.x; i < a.ppk * u.gh; i += blockDim.x) {
+    const int g = u.g0 + i / a.ppk, sub = i % a.ppk;
+    const int64_t pi = bwd_partial_index(a, u.z, u.hkv * p.gqa + g, u.kvb, 0) + sub;
     a.dn_part[pi] = v;
     a.db_part[pi] = v;
   }
@@ -266,7 +291,7 @@ __device__ __forceinline__ void bwd_chunk(const uint32_t (&sx)[W], const uint32_
   }
 }
 
-template <bool BF16>
+template <bool BF16, bool DET>
 __global__ void __launch_bounds__(512, 1)
     bwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ,
                      const __grid_constant__ CUtensorMap tmK,
@@ -303,6 +328,9 @@ __global__ void __launch_bounds__(512, 1)
   const int T_h = (L - q_start + C::BT - 1) / C::BT;  // query tiles per q-head
   const int T = T_h * unit.gh;
   const int zc = p.cu_seqlens ? 0 : z;
+  // Deterministic dq writes dn/db partials per query tile: start this slice's at zero (the
+  // __syncthreads below orders these writes before the P/dS warps' own).
+  if (DET) bwd_block_partials<BF16>(a, unit, seq_start, n0, L, false);
 
   if (threadIdx.x == 0) {
     mbar_init(bar(BB_KV), 1);
@@ -348,7 +376,8 @@ __global__ void __launch_bounds__(512, 1)
     // latency overlaps the wait for a free stage.
     float pl[C::BT / 32], pd[C::BT / 32];
     auto fetch_stats = [&](int t) {
-      const int g = t / T_h, tt = t - g * T_h;
+      int g, tt;
+      tile_coords(t, T_h, unit.gh, DET, g, tt);
       const int hq = hq0 + g;
       const int m0 = q_start + tt * C::BT;
 #pragma unroll
@@ -369,7 +398,8 @@ __global__ void __launch_bounds__(512, 1)
     fetch_stats(0);
     for (int t = 0; t < T; ++t) {
       const int st = t % C::STAGES, u = t / C::STAGES;
-      const int g = t / T_h, tt = t - g * T_h;
+      int g, tt;
+      tile_coords(t, T_h, unit.gh, DET, g, tt);
       const int hq = hq0 + g;
       const int m0 = q_start + tt * C::BT;
       bool ok = true;
@@ -528,11 +558,12 @@ __global__ void __launch_bounds__(512, 1)
       tmem_ld16(tS, sx);
       tmem_ld16(tP, dp);
     }
-    int st = 0, g = 0, tt = 0;  // ring stage, q-head within the group, tile within the head
+    // ring stage, q-head within the slice, query tile within the head (tile_coords order)
+    int st = 0, g = 0, tt = DET ? T_h - 1 : 0;
     for (int t = 0; ok && t < T; ++t) {
       const int dsb = t & 1;
       const int hq = hq0 + g;
-      if (tt == 0) {
+      if (DET || tt == 0) {  // a new q-head (the deterministic order changes head every tile)
         n = load_n(p, hq);
         nbs = n * bval * p.scale;
       }
@@ -607,7 +638,9 @@ __global__ void __launch_bounds__(512, 1)
           ok = false;
         }
       }
-      if (tt == T_h - 1) {  // end of q-head g: each warp writes its dn/db partial
+      // End of q-head g (deterministic order, where heads alternate: every tile): each warp
+      // writes its dn/db partial.
+      if (DET || tt == T_h - 1) {
         float x1 = (dn_acc[0].x + dn_acc[0].y) + (dn_acc[1].x + dn_acc[1].y);
         float x2 = (db_acc[0].x + db_acc[0].y) + (db_acc[1].x + db_acc[1].y);
 #pragma unroll
@@ -616,7 +649,7 @@ __global__ void __launch_bounds__(512, 1)
           x2 += __shfl_xor_sync(0xffffffffu, x2, o);
         }
         if (lane == 0) {
-          const int64_t pi = ((int64_t)z * p.Hq + hq) * (8 * a.nkv) + 8 * kvb + 4 * h + quad;
+          const int64_t pi = bwd_partial_index(a, z, hq, kvb, DET ? tt : 0) + 4 * h + quad;
           a.dn_part[pi] = x1 * kLn2;
           a.db_part[pi] = x2 * n * p.scale;
         }
@@ -624,7 +657,12 @@ __global__ void __launch_bounds__(512, 1)
         for (int i = 0; i < 2; ++i) dn_acc[i] = db_acc[i] = make_float2(0.f, 0.f);
       }
       st = st + 1 == C::STAGES ? 0 : st + 1;
-      if (++tt == T_h) {
+      if (DET) {
+        if (++g == unit.gh) {
+          g = 0;
+          --tt;
+        }
+      } else if (++tt == T_h) {
         tt = 0;
         ++g;
       }
@@ -668,11 +706,24 @@ __global__ void __launch_bounds__(512, 1)
       tmem_pin(v1);
       tc_fence_before();
       mbar_arrive(bar(BB_SM));  // dQ(t) is out of TMEM: counts toward SM(t + 1)
-      const int g = t / T_h, tt = t - g * T_h;
+      int g, tt;
+      tile_coords(t, T_h, unit.gh, DET, g, tt);
       const int hq = hq0 + g;
       const int m0 = q_start + tt * C::BT + quad * 32;
       const int row0 = p.cu_seqlens ? (int)((int64_t)hq * a.dq_rows + seq_start + m0)
                                     : (int)(((int64_t)z * p.Hq + hq) * a.dq_rows + m0);
+      // Deterministic dq: these 32 rows take their turn after key blocks 0 .. kvb - 1.
+      int* sem = DET ? a.dq_sem + (((int64_t)z * p.Hq + hq) * a.ntq + q_start / C::BT + tt) * 4 +
+                             quad
+                       : nullptr;
+      if (DET) {
+        bool okw = true;
+        if (lane == 0) okw = sem_wait_eq(sem, kvb, a.status);
+        if (!__shfl_sync(0xffffffffu, okw ? 1 : 0, 0)) {
+          ok = false;
+          break;
+        }
+      }
 #pragma unroll
       for (int hc = 0; hc < 2; ++hc) {
         const uint32_t(&v)[32] = hc ? v1 : v0;
@@ -689,6 +740,10 @@ __global__ void __launch_bounds__(512, 1)
           tma_reduce_add_2d(&tmDQ, stage_s, hc * 32, row0);
           bulk_commit();
         }
+      }
+      if (DET && lane == 0) {  // both adds performed, then the next key block's turn
+        bulk_wait0();
+        sem_release_next(sem);
       }
     }
     if (!ok) *abort_flag = 1;
@@ -711,13 +766,23 @@ __global__ void __launch_bounds__(512, 1)
 
 // Backward preprocess for the tensor-core path, one pass: delta = rowsum(O * dO) in fp32
 // (ssa_triton_kernel.py:267-298) and zeroing of the fp32 dQ accumulator rows (padding rows
-// included). D/8 threads per row, 16-byte loads; 2048/D rows per 256-thread block.
+// included) and, for deterministic dq, of the turn counters (sem_per_zh per sequence x q-head).
+// D/8 threads per row, 16-byte loads; 2048/D rows per 256-thread block.
 template <typename T, int D>
 __global__ void __launch_bounds__(256) bwd_preprocess_sm100_kernel(Problem p, TensorRef o,
                                                                    TensorRef dout, float* delta,
                                                                    float* dq_accum,
-                                                                   int64_t dq_rows) {
+                                                                   int64_t dq_rows, int* sem,
+                                                                   int sem_per_zh) {
   griddep_launch_dependents();  // the backward's setup may overlap this pass
+  if (sem && blockIdx.x == 0) {
+    const int nz = p.cu_seqlens ? p.B : 1;  // packed: grid row = q-head, every document
+    for (int zz = 0; zz < nz; ++zz) {
+      const int64_t base =
+          (int64_t)(p.cu_seqlens ? zz * p.Hq + (int)blockIdx.y : (int)blockIdx.y) * sem_per_zh;
+      for (int i = threadIdx.x; i < sem_per_zh; i += blockDim.x) sem[base + i] = 0;
+    }
+  }
   constexpr int TPR = D / 8, RPB = 256 / TPR;
   const int sub = threadIdx.x % TPR;
   const int rr = blockIdx.x * RPB + threadIdx.x / TPR;  // row within the head's accumulator
@@ -954,7 +1019,7 @@ enum Bwd128Bar : int {
   B2_COUNT = 18
 };
 
-template <bool BF16>
+template <bool BF16, bool DET>
 __global__ void __launch_bounds__(512, 1)
     bwd128_sm100_kernel(const __grid_constant__ CUtensorMap tmQ,
                         const __grid_constant__ CUtensorMap tmK,
@@ -1046,7 +1111,8 @@ __global__ void __launch_bounds__(512, 1)
       int last_tile = -1;
       float pl[2], pd[2];
       auto fetch_stats = [&](int t) {
-        const int g = t / T_h, tt = t - g * T_h;
+        int g, tt;
+        tile_coords(t, T_h, unit.gh, DET, g, tt);
         const int hq = hq0 + g;
         const int m0 = q_start + tt * C::BT;
 #pragma unroll
@@ -1064,7 +1130,8 @@ __global__ void __launch_bounds__(512, 1)
       fetch_stats(0);
       for (int t = 0; t < T; ++t) {
         const int st = t % C::STAGES, u = t / C::STAGES;
-        const int g = t / T_h, tt = t - g * T_h;
+        int g, tt;
+        tile_coords(t, T_h, unit.gh, DET, g, tt);
         const int hq = hq0 + g;
         const int m0 = q_start + tt * C::BT;
         bool ok = true;
@@ -1208,7 +1275,8 @@ __global__ void __launch_bounds__(512, 1)
     const int qmin = p.causal ? j : 0;
     for (int t = h; t < T; t += 2) {
       const int st = t % C::STAGES;
-      const int g = t / T_h, tt = t - g * T_h;
+      int g, tt;
+      tile_coords(t, T_h, unit.gh, DET, g, tt);
       const int hq = hq0 + g;
       n = load_n(p, hq);
       nbs = n * bval * p.scale;
@@ -1274,8 +1342,9 @@ __global__ void __launch_bounds__(512, 1)
       tc_fence_before();
       fence_proxy_async_smem();
       mbar_arrive(bar(B2_SM + h));
-      // this group's last tile of q-head g: write its per-warp dn/db partials
-      const bool head_end = (tt + 2 >= T_h);
+      // this group's last tile of q-head g (deterministic order, where heads alternate: every
+      // tile): write its per-warp dn/db partials
+      const bool head_end = DET || (tt + 2 >= T_h);
       if (head_end) {
         float x1 = (dn_acc[0].x + dn_acc[0].y) + (dn_acc[1].x + dn_acc[1].y);
         float x2 = (db_acc[0].x + db_acc[0].y) + (db_acc[1].x + db_acc[1].y);
@@ -1285,7 +1354,7 @@ __global__ void __launch_bounds__(512, 1)
           x2 += __shfl_xor_sync(0xffffffffu, x2, o);
         }
         if (lane == 0) {
-          const int64_t pi = ((int64_t)z * p.Hq + hq) * (8 * a.nkv) + 8 * kvb + 4 * h + quad;
+          const int64_t pi = bwd_partial_index(a, z, hq, kvb, DET ? tt : 0) + 4 * h + quad;
           a.dn_part[pi] = x1 * kLn2;
           a.db_part[pi] = x2 * n * p.scale;
         }
@@ -1336,14 +1405,32 @@ __global__ void __launch_bounds__(512, 1)
       for (int qi = 0; qi < 32; ++qi) stage[(32 + qi) * 32 + lane] = __uint_as_float(v1[qi]);
       fence_proxy_async_smem();
       __syncwarp();
+      bool okw = true;
       if (lane == 0) {
-        const int g = t / T_h, tt = t - g * T_h;
+        int g, tt;
+        tile_coords(t, T_h, unit.gh, DET, g, tt);
         const int hq = hq0 + g;
         const int m0 = q_start + tt * C::BT;
         const int row0 = p.cu_seqlens ? (int)((int64_t)hq * a.dq_rows + seq_start + m0)
                                       : (int)(((int64_t)z * p.Hq + hq) * a.dq_rows + m0);
-        tma_reduce_add_2d(&tmDQ, stage_s, quad * 32, row0);
-        bulk_commit();
+        // Deterministic dq: this warp's head dims of the tile take their turn after key blocks
+        // 0 .. kvb - 1, and pass it on once the add has been performed.
+        int* sem = DET ? a.dq_sem +
+                               (((int64_t)z * p.Hq + hq) * a.ntq + q_start / C::BT + tt) * 4 + quad
+                         : nullptr;
+        if (DET) okw = sem_wait_eq(sem, kvb, a.status);
+        if (okw) {
+          tma_reduce_add_2d(&tmDQ, stage_s, quad * 32, row0);
+          bulk_commit();
+          if (DET) {
+            bulk_wait0();
+            sem_release_next(sem);
+          }
+        }
+      }
+      if (!__shfl_sync(0xffffffffu, okw ? 1 : 0, 0)) {
+        ok = false;
+        break;
       }
     }
     if (!ok) *abort_flag = 1;
@@ -1365,9 +1452,9 @@ __global__ void __launch_bounds__(512, 1)
 }
 
 struct BwdLayout {
-  int nkv, hsplit;
+  int nkv, hsplit, ntq, ppk;
   int64_t dq_rows;
-  size_t dq_bytes, part_bytes, dkv_bytes, total;
+  size_t dq_bytes, part_bytes, dkv_bytes, sem_bytes, total;
 };
 
 constexpr int kNumSMs = 148;      // B200
@@ -1424,12 +1511,16 @@ BwdLayout bwd_layout(const Problem& p) {
     l.dq_rows = (int64_t)((p.N + 127) / 128) * 128;
     l.dq_bytes = al256(sizeof(float) * (size_t)p.B * p.Hq * l.dq_rows * p.D);
   }
-  l.part_bytes = al256(sizeof(float) * (size_t)p.B * p.Hq * 8 * l.nkv);
-  l.hsplit = choose_hsplit(p, p.D == 128 ? 64 : 128);
+  const int bt = p.D == 128 ? 64 : 128;  // query tile rows of the kernel
+  l.ntq = (p.max_seqlen + bt - 1) / bt;
+  l.ppk = p.det ? 8 * l.ntq : 8;
+  l.part_bytes = al256(sizeof(float) * (size_t)p.B * p.Hq * l.ppk * l.nkv);
+  l.sem_bytes = p.det ? al256(sizeof(int) * (size_t)p.B * p.Hq * l.ntq * 4) : 0;
+  l.hsplit = choose_hsplit(p, bt);
   l.dkv_bytes = l.hsplit > 1 ? al256(sizeof(float) * (size_t)p.B * p.Hkv * l.nkv * l.hsplit * 2 *
                                      128 * p.D)
                              : 0;
-  l.total = l.dq_bytes + 2 * l.part_bytes + l.dkv_bytes;
+  l.total = l.dq_bytes + 2 * l.part_bytes + l.dkv_bytes + l.sem_bytes;
   return l;
 }
 
@@ -1464,11 +1555,15 @@ int run_bwd(const Problem& p, TensorRef q, TensorRef k, TensorRef v, TensorRef o
   a.dkv_part = lay.hsplit > 1
                    ? reinterpret_cast<float*>(w + lay.dq_bytes + 2 * lay.part_bytes)
                    : nullptr;
+  a.ppk = lay.ppk;
+  a.ntq = lay.ntq;
+  a.dq_sem = p.det ? reinterpret_cast<int*>(w + lay.dq_bytes + 2 * lay.part_bytes + lay.dkv_bytes)
+                   : nullptr;
   {
     using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
     dim3 gp((unsigned)((lay.dq_rows + 31) / 32), p.cu_seqlens ? p.Hq : p.B * p.Hq);
     bwd_preprocess_sm100_kernel<T, 64><<<gp, 256, 0, st>>>(p, out, dout, delta, a.dq_accum,
-                                                            lay.dq_rows);
+                                                            lay.dq_rows, a.dq_sem, 4 * lay.ntq);
     note_launches(1);
   }
   // dQ accumulator as a 2-D fp32 tensor [rows][64] for the drain's tiled reduce-adds:
@@ -1487,7 +1582,7 @@ int run_bwd(const Problem& p, TensorRef q, TensorRef k, TensorRef v, TensorRef o
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return SSA_ERR_CUDA;
   }
-  auto kern = bwd_sm100_kernel<BF16>;
+  auto kern = p.det ? bwd_sm100_kernel<BF16, true> : bwd_sm100_kernel<BF16, false>;
   if (set_smem_limit_once(reinterpret_cast<const void*>(kern), (int)C::SMEM_BYTES) != SSA_OK)
     return SSA_ERR_CUDA;
   const long long grid = (long long)lay.nkv * p.B * p.Hkv * lay.hsplit;
@@ -1497,7 +1592,7 @@ int run_bwd(const Problem& p, TensorRef q, TensorRef k, TensorRef v, TensorRef o
   note_launches(1);
   using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
   return launch_dq_convert_dndb<T, 64>(p, a.dq_accum, a.dq_rows, dq, a.dn_part, a.db_part,
-                                       8 * lay.nkv, dn, db, a, st);
+                                       lay.ppk * lay.nkv, dn, db, a, st);
 }
 
 template <bool BF16>
@@ -1532,10 +1627,14 @@ int run_bwd128(const Problem& p, TensorRef q, TensorRef k, TensorRef v, TensorRe
   a.dkv_part = lay.hsplit > 1
                    ? reinterpret_cast<float*>(w + lay.dq_bytes + 2 * lay.part_bytes)
                    : nullptr;
+  a.ppk = lay.ppk;
+  a.ntq = lay.ntq;
+  a.dq_sem = p.det ? reinterpret_cast<int*>(w + lay.dq_bytes + 2 * lay.part_bytes + lay.dkv_bytes)
+                   : nullptr;
   {
     dim3 gp((unsigned)((lay.dq_rows + 15) / 16), p.cu_seqlens ? p.Hq : p.B * p.Hq);
     bwd_preprocess_sm100_kernel<T, 128><<<gp, 256, 0, st>>>(p, out, dout, delta, a.dq_accum,
-                                                             lay.dq_rows);
+                                                             lay.dq_rows, a.dq_sem, 4 * lay.ntq);
   }
   {  // dQ accumulator as 2-D fp32 [rows][128]; {32 head dims x 64 queries} boxes, no swizzle
     auto enc = tmap_encoder();
@@ -1550,14 +1649,14 @@ int run_bwd128(const Problem& p, TensorRef q, TensorRef k, TensorRef v, TensorRe
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return SSA_ERR_CUDA;
   }
-  auto kern = bwd128_sm100_kernel<BF16>;
+  auto kern = p.det ? bwd128_sm100_kernel<BF16, true> : bwd128_sm100_kernel<BF16, false>;
   if (set_smem_limit_once(reinterpret_cast<const void*>(kern), (int)C::SMEM_BYTES) != SSA_OK)
     return SSA_ERR_CUDA;
   const long long grid = (long long)lay.nkv * p.B * p.Hkv * lay.hsplit;
   kern<<<(unsigned)grid, C::THREADS, C::SMEM_BYTES, st>>>(tq, tk, tv, tdo, tdq, a);
   note_launches(2);
   return launch_dq_convert_dndb<T, 128>(p, a.dq_accum, a.dq_rows, dq, a.dn_part, a.db_part,
-                                        8 * lay.nkv, dn, db, a, st);
+                                        lay.ppk * lay.nkv, dn, db, a, st);
 }
 
 }  // namespace sm100

@@ -50,6 +50,23 @@ def golden_qkv(meta, arrays, device="cpu", dtype=None):
     return q, k, v, do.to(device=device, dtype=dtype)
 
 
+def to_queue(obj) -> bytes:
+    """Serialise a worker's result (tensors of any dtype included) for a multiprocessing queue.
+    Tensors put on a queue directly travel as shared-memory handles that the parent can no longer
+    open once the worker has exited; these bytes travel by value."""
+    import io
+    import torch
+    buf = io.BytesIO()
+    torch.save(obj, buf)
+    return buf.getvalue()
+
+
+def from_queue(data: bytes):
+    import io
+    import torch
+    return torch.load(io.BytesIO(data), weights_only=False)
+
+
 @pytest.fixture(scope="session")
 def cuda_device():
     import torch

@@ -190,3 +190,33 @@ def test_layout_rule_of_the_wrappers():
         assert _prep(t, 0) is t  # the generic kernels only need a unit D stride
     c = _prep(d_strided, 0)
     assert c is not d_strided and c.stride(-1) == 1 and torch.equal(c, d_strided)
+
+
+def test_ctypes_structs_match_the_c_header(tmp_path):
+    """The ctypes mirrors of ssa_problem_t / ssa_tensor_t have the C header's field offsets and
+    sizes (compiled here with gcc against include/ssa_b200.h)."""
+    import ctypes
+    import shutil
+    import subprocess
+    from SSA import _lib
+    gcc = shutil.which("gcc")
+    if gcc is None:
+        pytest.skip("gcc not available")
+    fields = [f for f, _ in _lib.SsaProblem._fields_]
+    prog = ["#include <stdio.h>", "#include <stddef.h>", '#include "ssa_b200.h"',
+            "int main(void) {",
+            '  printf("problem %zu\\n", sizeof(ssa_problem_t));',
+            '  printf("tensor %zu\\n", sizeof(ssa_tensor_t));']
+    for f in fields:
+        prog.append(f'  printf("{f} %zu\\n", offsetof(ssa_problem_t, {f}));')
+    prog += ["  return 0;", "}"]
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(prog) + "\n")
+    exe = tmp_path / "layout"
+    subprocess.run([gcc, "-I", str(REPO / "include"), str(src), "-o", str(exe)], check=True)
+    out = dict(line.split() for line in subprocess.run([str(exe)], capture_output=True,
+                                                       text=True, check=True).stdout.splitlines())
+    assert int(out["problem"]) == ctypes.sizeof(_lib.SsaProblem)
+    assert int(out["tensor"]) == ctypes.sizeof(_lib.SsaTensor)
+    for f in fields:
+        assert int(out[f]) == getattr(_lib.SsaProblem, f).offset, f

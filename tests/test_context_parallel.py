@@ -16,6 +16,8 @@ import pytest
 import torch
 import torch.multiprocessing as mp
 
+from conftest import from_queue, to_queue
+
 REPO = Path(__file__).resolve().parent.parent
 
 
@@ -55,7 +57,7 @@ def _cpu_worker(rank, world, port, q, k, v, do, n, b, scale, out_q):
     out, lse = ring_ssa_forward(ql, kl, vl, scale, n, b, pair_fwd=pair_fwd)
     dq, dk, dv, dn, db = ring_ssa_backward(ql, kl, vl, out, dol, lse, scale, n, b,
                                            pair_bwd=pair_bwd)
-    out_q.put((rank, out, dq, dk, dv, dn, db))
+    out_q.put(to_queue((rank, out, dq, dk, dv, dn, db)))
     out_q.close()
     out_q.join_thread()
     dist.barrier()
@@ -82,7 +84,7 @@ def test_ring_matches_full_sequence_cpu(per_head, world):
           for r in range(world)]
     for p in ps:
         p.start()
-    res = sorted((out_q.get(timeout=180) for _ in ps), key=lambda t: t[0])
+    res = sorted((from_queue(out_q.get(timeout=180)) for _ in ps), key=lambda t: t[0])
     for p in ps:
         p.join(timeout=60)
         assert p.exitcode == 0
@@ -108,7 +110,7 @@ def _gpu_worker(rank, world, port, q, k, v, do, n, b, scale, out_q):
     out, lse = ring_ssa_forward(ql, kl, vl, scale, n.to(dev), b.to(dev))
     dq, dk, dv, dn, db = ring_ssa_backward(ql, kl, vl, out, dol, lse, scale, n.to(dev), b.to(dev))
     torch.cuda.synchronize()
-    out_q.put((rank, out.cpu(), dq.cpu(), dk.cpu(), dv.cpu(), dn.cpu(), db.cpu()))
+    out_q.put(to_queue((rank, out.cpu(), dq.cpu(), dk.cpu(), dv.cpu(), dn.cpu(), db.cpu())))
     out_q.close()
     out_q.join_thread()
     dist.barrier(device_ids=[rank])
@@ -137,7 +139,7 @@ def test_ring_on_two_gpus_matches_single_gpu():
           for r in range(world)]
     for p in ps:
         p.start()
-    res = sorted((out_q.get(timeout=300) for _ in ps), key=lambda t: t[0])
+    res = sorted((from_queue(out_q.get(timeout=300)) for _ in ps), key=lambda t: t[0])
     for p in ps:
         p.join(timeout=120)
         assert p.exitcode == 0

@@ -12,6 +12,8 @@ import pytest
 import torch
 import torch.multiprocessing as mp
 
+from conftest import from_queue, to_queue
+
 REPO = Path(__file__).resolve().parent.parent
 
 
@@ -60,7 +62,7 @@ def _worker(rank, world, port, q, k, v, do, n, b, out_q):
     dn2, db2 = pair[:dn.numel()].view(dn.shape), pair[dn.numel()]
     allreduce_ssa_param_grads(dn2, db2, async_op=True).wait()
     assert torch.equal(dn2, dn) and torch.equal(db2, db)
-    out_q.put((rank, dn, db))
+    out_q.put(to_queue((rank, dn, db)))
     dist.barrier()
     dist.destroy_process_group()
 
@@ -83,7 +85,7 @@ def test_sharded_dn_db_allreduce_matches_full_batch():
              for r in range(2)]
     for p in procs:
         p.start()
-    results = [out_q.get(timeout=120) for _ in procs]
+    results = [from_queue(out_q.get(timeout=120)) for _ in procs]
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0

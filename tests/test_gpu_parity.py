@@ -398,6 +398,80 @@ def test_bit_deterministic(dtype, cuda_device):
             assert torch.equal(r1[name], r2[name]), name
 
 
+@pytest.mark.parametrize("B,Hq,Hkv,N,D,causal", [
+    (2, 8, 2, 1024, 64, True),     # 8 key blocks per sequence: long chains of ordered dQ adds
+    (1, 8, 2, 700, 64, False),     # non-causal: every key block adds to every tile; q-head slices
+    (1, 4, 2, 640, 128, True),     # D = 128 kernel (64-query tiles)
+])
+def test_deterministic_dq_is_bit_identical(B, Hq, Hkv, N, D, causal, cuda_device):
+    """deterministic=True: every dQ tile's contributions are added in ascending key-block order,
+    so two identical runs give bit-identical dq as well as out, lse, dk, dv, dn, db
+    (check_ssa_triton_parity.py:507-562, atol 0), and the result matches the oracle."""
+    K = _api()
+    q = seeded((B, Hq, N, D), 401, 0.5).to(cuda_device)
+    k = seeded((B, Hkv, N, D), 402, 0.5).to(cuda_device)
+    v = seeded((B, Hkv, N, D), 403, 0.5).to(cuda_device)
+    do = seeded((B, Hq, N, D), 404).to(cuda_device)
+    n = (0.3 + 0.3 * torch.rand(Hq, generator=torch.Generator().manual_seed(405))).to(cuda_device)
+    b = torch.tensor(0.8, device=cuda_device)
+    scale = D ** -0.5
+    runs = []
+    for _ in range(3):
+        out, m = K.ssa_flash_attn_forward(q, k, v, scale, n, b, causal=causal)
+        grads = K.ssa_flash_attn_backward(q, k, v, out, do, m, scale, n, b, causal=causal,
+                                          deterministic=True)
+        torch.cuda.synchronize()
+        runs.append((out, m) + tuple(grads))
+    for r in runs[1:]:
+        for name, a, b2 in zip(("out", "m", "dq", "dk", "dv", "dn", "db"), runs[0], r):
+            assert torch.equal(a, b2), f"{name} differs between deterministic runs"
+    ref = ssa_reference_grads(q.cpu(), k.cpu(), v.cpu(), scale, n.cpu(), b.cpu(), do.cpu(), causal)
+    for name, got in zip(("out", "dq", "dk", "dv"), (runs[0][0],) + runs[0][2:5]):
+        assert_lowp_close(name, got, ref[name])
+    assert_scalar_close("dn", runs[0][5], ref["dn"])
+    assert_scalar_close("db", runs[0][6], ref["db"])
+    # the default (unordered) mode computes the same gradients up to rounding
+    dq_fast = K.ssa_flash_attn_backward(q, k, v, runs[0][0], do, runs[0][1], scale, n, b,
+                                        causal=causal, deterministic=False)[0]
+    d = (dq_fast.float() - runs[0][2].float()).abs()
+    assert (d <= runs[0][2].float().abs() * 2 ** -7 + 1e-6).all()
+
+
+def test_deterministic_dq_packed_documents(cuda_device):
+    """Deterministic dq on packed documents (per-document key blocks and query tiles), through
+    the environment switch SSA_DETERMINISTIC=1 and the autograd Function."""
+    import os
+    from SSA.ssa_flash_attention import ssa_flash_attn_varlen_func
+    lens = [300, 1000, 77, 513]
+    T, Hq, Hkv, D = sum(lens), 8, 2, 64
+    cu = torch.tensor([0] + list(torch.tensor(lens).cumsum(0)), dtype=torch.int32)
+    q = seeded((T, Hq, D), 411, 0.5)
+    k = seeded((T, Hkv, D), 412, 0.5)
+    v = seeded((T, Hkv, D), 413, 0.5)
+    do = seeded((T, Hq, D), 414)
+    n, b = torch.tensor(0.6), torch.tensor(0.8)
+    dev = cuda_device
+    old = os.environ.get("SSA_DETERMINISTIC")
+    os.environ["SSA_DETERMINISTIC"] = "1"
+    try:
+        grads = []
+        for _ in range(3):
+            qd = q.to(dev).requires_grad_(True)
+            out = ssa_flash_attn_varlen_func(qd, k.to(dev), v.to(dev), cu.to(dev), max(lens),
+                                             D ** -0.5, n.to(dev), b.to(dev), True)
+            out.backward(do.to(dev))
+            torch.cuda.synchronize()
+            grads.append(qd.grad.clone())
+    finally:
+        if old is None:
+            os.environ.pop("SSA_DETERMINISTIC")
+        else:
+            os.environ["SSA_DETERMINISTIC"] = old
+    assert torch.equal(grads[0], grads[1]) and torch.equal(grads[0], grads[2])
+    ref = ssa_reference_grads_varlen(q, k, v, cu, D ** -0.5, n, b, do, True)
+    assert_lowp_close("dq", grads[0], ref["dq"])
+
+
 def test_autograd_function_and_module(cuda_device):
     from SSA.ssa_flash_attention import ssa_flash_attention
     from SSA.ssa_triton_attention import SSAAttentionConfig, SSATritonAttention

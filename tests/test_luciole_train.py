@@ -77,7 +77,9 @@ def _ddp_worker(rank, world, port, out_q):
         tok = torch.randint(0, cfg.vocab, (2, 33), generator=g)
         LT.train_step(ddp, opt, tok[:, :-1], tok[:, 1:])
     flat = torch.cat([p.detach().reshape(-1) for p in model.parameters()])
-    out_q.put((rank, flat))
+    # a numpy copy travels by value (a tensor would travel as a shared-memory handle, which the
+    # parent cannot open once this process has exited)
+    out_q.put((rank, flat.numpy().copy()))
     dist.barrier()
     dist.destroy_process_group()
 
@@ -93,7 +95,7 @@ def test_ddp_two_gloo_ranks_keep_replicas_identical():
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
-    assert torch.equal(res[0], res[1])
+    assert (res[0] == res[1]).all()
 
 
 @pytest.mark.gpu

@@ -74,6 +74,17 @@ __device__ __forceinline__ float load_n(const Problem& p, int hq) {
   return __ldg(p.n_ptr + (p.n_per_head ? hq : 0));
 }
 
+// The device status word (non-zero after an expired bounded wait), read by one thread and shared
+// with the block: every thread of every block reading the one word directly piles the loads onto
+// a single L2 slice (that cost the dq conversion a third of its time on B200). Called by every
+// thread of the block at a point they all reach; contains a __syncthreads.
+__device__ __forceinline__ bool block_status_failed(const unsigned int* status) {
+  __shared__ unsigned int s_status;
+  if (threadIdx.x == 0) s_status = *reinterpret_cast<const volatile unsigned int*>(status);
+  __syncthreads();
+  return s_status != 0;
+}
+
 // Quiet NaN written into the outputs of a kernel that skipped its work because a bounded device
 // wait expired (in this launch or an earlier one): a caller that never reads the status word still
 // sees the failure as NaN in out / lse / dq / dk / dv / dn / db instead of stale memory.

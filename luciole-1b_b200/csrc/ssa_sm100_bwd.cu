@@ -320,7 +320,7 @@ __global__ void __launch_bounds__(512, 1)
   const int n0 = kvb * C::BN;
   // Block-uniform exits: a block past the sequence end has nothing to add; after a device
   // timeout recorded by an earlier launch, this block's outputs are NaN.
-  if (n0 >= L || *reinterpret_cast<volatile unsigned int*>(a.status) != 0) {
+  if (n0 >= L || block_status_failed(a.status)) {
     bwd_block_partials<BF16>(a, unit, seq_start, n0, L, n0 < L);
     return;
   }
@@ -849,7 +849,7 @@ __global__ void __launch_bounds__(256) dq_convert_kernel(Problem p, const float*
                                                          DndbArgs r) {
   griddep_wait();  // launched programmatically behind the backward kernel
   // After a device timeout (this backward's or an earlier launch's) dq, dn and db are NaN.
-  const bool failed = *reinterpret_cast<const volatile unsigned int*>(r.status) != 0;
+  const bool failed = block_status_failed(r.status);
   if ((int)blockIdx.y < r.rows) {
     __shared__ double red[256];
     const int nred = (p.n_per_head ? p.Hq : 1) + 1;
@@ -1048,7 +1048,7 @@ __global__ void __launch_bounds__(512, 1)
   const int n0 = kvb * C::BN;
   // Block-uniform exits: a block past the sequence end has nothing to add; after a device
   // timeout recorded by an earlier launch, this block's outputs are NaN.
-  if (n0 >= L || *reinterpret_cast<volatile unsigned int*>(a.status) != 0) {
+  if (n0 >= L || block_status_failed(a.status)) {
     bwd_block_partials<BF16>(a, unit, seq_start, n0, L, n0 < L);
     return;
   }

@@ -114,7 +114,7 @@ __global__ void __launch_bounds__(192, 2)
   // Block-uniform exits, before any barrier or TMEM allocation: nothing to do, or an earlier
   // launch already recorded a device-side timeout (this tile's out and lse rows are then NaN).
   if (m0 >= L) return;
-  if (*reinterpret_cast<volatile unsigned int*>(a.status) != 0) {
+  if (block_status_failed(a.status)) {
     nan_fill_rows16<BF16>(a.o, p, z, hq, seq_start, m0, min(m0 + C::BM, L), a.lse);
     return;
   }

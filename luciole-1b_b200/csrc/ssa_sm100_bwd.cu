@@ -291,12 +291,6 @@ __device__ __forceinline__ void bwd_chunk(const uint32_t (&sx)[W], const uint32_
   }
 }
 
-// Half 1 of each D = 64 tile runs its chunks offset by 8 queries from half 0 (see the P/dS loop).
-#ifndef SSA_BWD_HALF1_OFFSET
-#define SSA_BWD_HALF1_OFFSET 1
-#endif
-constexpr bool kHalf1Offset = SSA_BWD_HALF1_OFFSET != 0;
-
 template <bool BF16, bool DET>
 __global__ void __launch_bounds__(512, 1)
     bwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ,
@@ -561,13 +555,8 @@ __global__ void __launch_bounds__(512, 1)
     bool ok = wait_tile(0);
     if (ok) {  // chunk 0 of tile 0; later tiles' chunk 0 is fetched after the previous tile's SM
       tc_fence_after();
-      if (!kHalf1Offset || h == 0) {
-        tmem_ld16(tS, sx);
-        tmem_ld16(tP, dp);
-      } else {
-        tmem_ld8(tS, sx);
-        tmem_ld8(tP, dp);
-      }
+      tmem_ld16(tS, sx);
+      tmem_ld16(tP, dp);
     }
     // ring stage, q-head within the slice, query tile within the head (tile_coords order)
     int st = 0, g = 0, tt = DET ? T_h - 1 : 0;
@@ -587,92 +576,54 @@ __global__ void __launch_bounds__(512, 1)
       tmem_ld_wait_only();
       tmem_pin_n(sx);
       tmem_pin_n(dp);
-      // Chunks of 16 queries (16-wide chunks leave the compiler registers to overlap more element
-      // pairs than 32-wide ones). Chunk k + 1's S / dP loads are issued after chunk k has been
-      // computed and are in flight while chunk k's P^T and dS^T are stored. After the last chunk
-      // the tile's SM arrival goes first (the grads MMAs wait on it), then the next tile's first
-      // chunk is loaded. Half 0 runs chunks 16 x 4; half 1 runs 8, 16, 16, 16, 8 (kHalf1Offset):
-      // the two warps sharing an SM sub-partition then change between their special-function
-      // passes and their FMA pass at different times instead of in lock-step.
-      auto step = [&](auto off_c, auto w_c, auto noff_c, auto nw_c, auto idx_c, auto nch_c) {
-        constexpr int OFF = decltype(off_c)::value, W = decltype(w_c)::value;
-        constexpr int NOFF = decltype(noff_c)::value, NW = decltype(nw_c)::value;
-        constexpr int IDX = decltype(idx_c)::value, NCH = decltype(nch_c)::value;
-        uint32_t pk[W / 2], dk[W / 2];
-        const uint32_t(&cs)[W] = *reinterpret_cast<const uint32_t(*)[W]>(&sx[0]);
-        const uint32_t(&cd)[W] = *reinterpret_cast<const uint32_t(*)[W]>(&dp[0]);
+      // 4 chunks of 16 queries (16-wide chunks leave the compiler registers to overlap more
+      // element pairs than 32-wide ones). Chunk c + 1's S / dP loads are issued after chunk c
+      // has been computed and are in flight while chunk c's P^T and dS^T are stored. After
+      // chunk 3 the tile's SM arrival goes first (the grads MMAs wait on it), then the next
+      // tile's chunk 0 is loaded.
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        uint32_t pk[8], dk[8];
         // A chunk masked for every row of this warp (the lower part of a diagonal tile, or past
         // the sequence end) has P = dS = 0: its transform is skipped.
-        const bool dead = !full && ((p.causal && mh + OFF + W - 1 < n0 + quad * 32) ||
-                                    mh + OFF >= L || n0 + quad * 32 >= L);
+        const bool dead = !full && ((p.causal && mh + c * 16 + 15 < n0 + quad * 32) ||
+                                    mh + c * 16 >= L || n0 + quad * 32 >= L);
         if (dead) {
 #pragma unroll
-          for (int i = 0; i < W / 2; ++i) pk[i] = dk[i] = 0u;
+          for (int i = 0; i < 8; ++i) pk[i] = dk[i] = 0u;
         } else if (full)
-          bwd_chunk<W, BF16, false, true>(cs, cd, lrow + OFF, drow + OFF, n, cb, nbs, mh + OFF,
-                                          qmin, L, j < L, dn_acc, db_acc, pk, dk);
+          bwd_chunk<16, BF16, false, true>(sx, dp, lrow + c * 16, drow + c * 16, n, cb, nbs,
+                                           mh + c * 16, qmin, L, j < L, dn_acc, db_acc, pk, dk);
         else
-          bwd_chunk<W, BF16, true, true>(cs, cd, lrow + OFF, drow + OFF, n, cb, nbs, mh + OFF,
-                                         qmin, L, j < L, dn_acc, db_acc, pk, dk);
-        if constexpr (IDX + 1 < NCH) {
-          if constexpr (NW == 16) {
-            tmem_ld16(tS + NOFF, sx);
-            tmem_ld16(tP + NOFF, dp);
-          } else {
-            tmem_ld8(tS + NOFF, sx);
-            tmem_ld8(tP + NOFF, dp);
+          bwd_chunk<16, BF16, true, true>(sx, dp, lrow + c * 16, drow + c * 16, n, cb, nbs,
+                                          mh + c * 16, qmin, L, j < L, dn_acc, db_acc, pk, dk);
+        if (c < 3) {
+          tmem_ld16(tS + 16 * (c + 1), sx);
+          tmem_ld16(tP + 16 * (c + 1), dp);
+          if (c == 0) {
+            // dV(t-1) must have read this half's P^T columns before they are rewritten.
+            bool okb = t == 0 || mbar_wait(bar(BB_BF), (t - 1) & 1, a.status);
+            if (!__all_sync(0xffffffffu, okb)) *abort_flag = 1;
+            tc_fence_after();
           }
         }
-        if constexpr (IDX == 0) {
-          // dV(t-1) must have read this half's P^T columns before they are rewritten.
-          bool okb = t == 0 || mbar_wait(bar(BB_BF), (t - 1) & 1, a.status);
-          if (!__all_sync(0xffffffffu, okb)) *abort_flag = 1;
-          tc_fence_after();
-        }
-        if constexpr (W == 16)
-          tmem_st8(tPT + OFF / 2, *reinterpret_cast<const uint32_t(*)[8]>(&pk[0]));
-        else
-          tmem_st4(tPT + OFF / 2, *reinterpret_cast<const uint32_t(*)[4]>(&pk[0]));
+        tmem_st8(tPT + c * 8, pk);
         // dS^T row r of this half's slab: 16-byte chunks, 128-byte swizzle (chunk ^ (row & 7))
 #pragma unroll
-        for (int q2 = 0; q2 < W / 8; ++q2) {
-          const int chunk = OFF / 8 + q2;
+        for (int q2 = 0; q2 < 2; ++q2) {
+          const int chunk = c * 2 + q2;
           *reinterpret_cast<uint4*>(dsrow + ((chunk ^ (r & 7)) << 4)) =
               make_uint4(dk[q2 * 4], dk[q2 * 4 + 1], dk[q2 * 4 + 2], dk[q2 * 4 + 3]);
         }
-        if constexpr (IDX + 1 < NCH) {
+        if (c < 3) {
           tmem_ld_wait_only();
           tmem_pin_n(sx);
           tmem_pin_n(dp);
-          if constexpr (IDX + 2 == NCH) {
+          if (c == 2) {
             tc_fence_before();
             mbar_arrive(bar(BB_SC));  // this tile's S^T / dP^T columns may now be overwritten
           }
         }
-      };
-      using I0 = std::integral_constant<int, 0>;
-      using I8 = std::integral_constant<int, 8>;
-      using I16 = std::integral_constant<int, 16>;
-      if (!kHalf1Offset || h == 0) {
-        using I4 = std::integral_constant<int, 4>;
-        step(I0{}, I16{}, I16{}, I16{}, I0{}, I4{});
-        step(I16{}, I16{}, std::integral_constant<int, 32>{}, I16{},
-             std::integral_constant<int, 1>{}, I4{});
-        step(std::integral_constant<int, 32>{}, I16{}, std::integral_constant<int, 48>{}, I16{},
-             std::integral_constant<int, 2>{}, I4{});
-        step(std::integral_constant<int, 48>{}, I16{}, I0{}, I16{},
-             std::integral_constant<int, 3>{}, I4{});
-      } else {
-        using I5 = std::integral_constant<int, 5>;
-        step(I0{}, I8{}, I8{}, I16{}, I0{}, I5{});
-        step(I8{}, I16{}, std::integral_constant<int, 24>{}, I16{},
-             std::integral_constant<int, 1>{}, I5{});
-        step(std::integral_constant<int, 24>{}, I16{}, std::integral_constant<int, 40>{}, I16{},
-             std::integral_constant<int, 2>{}, I5{});
-        step(std::integral_constant<int, 40>{}, I16{}, std::integral_constant<int, 56>{}, I8{},
-             std::integral_constant<int, 3>{}, I5{});
-        step(std::integral_constant<int, 56>{}, I8{}, I0{}, I8{},
-             std::integral_constant<int, 4>{}, I5{});
       }
       tmem_st_wait();
       tc_fence_before();
@@ -681,13 +632,8 @@ __global__ void __launch_bounds__(512, 1)
       if (t + 1 < T) {
         if (wait_tile(t + 1)) {
           tc_fence_after();
-          if (!kHalf1Offset || h == 0) {
-            tmem_ld16(tS, sx);
-            tmem_ld16(tP, dp);
-          } else {
-            tmem_ld8(tS, sx);
-            tmem_ld8(tP, dp);
-          }
+          tmem_ld16(tS, sx);
+          tmem_ld16(tP, dp);
         } else {
           ok = false;
         }

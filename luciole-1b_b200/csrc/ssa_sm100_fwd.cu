@@ -5,15 +5,13 @@
 // (= n * sign(s) * log1p(b|s|) * log2 e, :96-107), an online base-2 normaliser (:110-113),
 // O = P V / l and M = m + log2 l (:248-255).
 //
-// One CTA = one 128-row query tile of one (sequence, q-head). Two warpgroups:
+// One CTA = one 128-row query tile of one (sequence, q-head). 6 warps:
 //   warp 0      TMEM allocator + TMA producer (Q once, K/V through a 2-stage ring)
 //   warp 1      MMA issuer: S = Q K^T (SS form, fp32 in TMEM), O += P V (TS form: P read
 //               straight from TMEM). P has its own columns, so S_{j+1} is issued as soon as the
 //               softmax warps hold S_j in registers and runs under their work on block j.
-//   warps 2..3  idle (they complete the control warpgroup, whose registers setmaxnreg lowers)
-//   warps 4..7  one thread per query row: tcgen05.ld its S row, SSA transform, running max
-//               and sum, P (bf16/f16) written to TMEM, O correction, epilogue; setmaxnreg raises
-//               them to 200 registers (every warp would otherwise get the launch's 128).
+//   warps 2..5  one thread per query row: tcgen05.ld its S row, SSA transform, running max
+//               and sum, P (bf16/f16) written to TMEM, O correction, epilogue.
 // Two CTAs share an SM (TMEM 2 x 256 columns, ~81 KB shared memory each), so one CTA's
 // transcendental work overlaps the other's tensor-core work.
 //
@@ -47,16 +45,6 @@ constexpr int kEmuPairs = D == 128 ? 1 : 0;
 template <int D>
 constexpr bool kLogFirst = D == 64;
 
-// Warp roles on two warpgroups (1): warps 0..3 control (producer, MMA issuer, two idle), warps
-// 4..7 softmax, so setmaxnreg can take registers from the control warps (kFwdRegsCtrl) and give
-// them to the softmax warps (kFwdRegsSoftmax); per CTA 128 x 56 + 128 x 200 = 256 threads x 128.
-// (0): six warps, every warp at the launch's 168 registers.
-#ifndef SSA_FWD_WARPGROUPS
-#define SSA_FWD_WARPGROUPS 1
-#endif
-constexpr bool kFwdWG = SSA_FWD_WARPGROUPS != 0;
-constexpr uint32_t kFwdRegsCtrl = 56, kFwdRegsSoftmax = 200;
-
 template <int D>
 struct FwdCfg {
   static constexpr int BM = 128;
@@ -74,7 +62,7 @@ struct FwdCfg {
   static constexpr uint32_t COL_S = 0;            // S (fp32, BN columns)
   static constexpr uint32_t COL_P = BN;           // P (packed 16-bit, BN / 2 columns)
   static constexpr uint32_t COL_O = BN + BN / 2;  // O accumulator (fp32, D columns)
-  static constexpr int THREADS = kFwdWG ? 256 : 192;
+  static constexpr int THREADS = 192;
   static_assert(BN + BN / 2 + D <= (int)TMEM_COLS, "TMEM budget");
 };
 
@@ -100,7 +88,7 @@ enum FwdBar : int {
 };
 
 template <int D, bool BF16>
-__global__ void __launch_bounds__(kFwdWG ? 256 : 192, 2)
+__global__ void __launch_bounds__(192, 2)
     fwd_sm100_kernel(const __grid_constant__ CUtensorMap tmQ,
                      const __grid_constant__ CUtensorMap tmK,
                      const __grid_constant__ CUtensorMap tmV, const FwdArgs a) {
@@ -159,9 +147,7 @@ __global__ void __launch_bounds__(kFwdWG ? 256 : 192, 2)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (kFwdWG ? warp < 4 : warp < 2) {
-   if constexpr (kFwdWG) regs_dec<kFwdRegsCtrl>();
-   if (warp == 0) {
+  if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
     if (lane == 0) {
       prefetch_tmap(&tmQ);
@@ -259,9 +245,7 @@ __global__ void __launch_bounds__(kFwdWG ? 256 : 192, 2)
       mma_commit_p(bar(FB_END), leader);  // all MMAs of this CTA retired before TMEM is freed
       mbar_wait(bar(FB_END), 0, a.status);
     }
-   }
   } else {
-    if constexpr (kFwdWG) regs_inc<kFwdRegsSoftmax>();
     // ------------------------------------------------------------------ softmax rows
     const int quad = warp & 3;
     const int r = quad * 32 + lane;

@@ -318,10 +318,11 @@ __global__ void __launch_bounds__(512, 1)
   int seq_start, L;
   seq_bounds(p, z, seq_start, L);
   const int n0 = kvb * C::BN;
-  // Block-uniform exits: a block past the sequence end has nothing to add; after a device
-  // timeout recorded by an earlier launch, this block's outputs are NaN.
-  if (n0 >= L || block_status_failed(a.status)) {
-    bwd_block_partials<BF16>(a, unit, seq_start, n0, L, n0 < L);
+  // Block-uniform exit: a block past the sequence end has nothing to add. (A device timeout
+  // recorded by an earlier launch is checked during the set-up below: the block then skips its
+  // work and writes NaN.)
+  if (n0 >= L) {
+    bwd_block_partials<BF16>(a, unit, seq_start, n0, L, false);
     return;
   }
   const int q_start = p.causal ? n0 : 0;
@@ -332,7 +333,11 @@ __global__ void __launch_bounds__(512, 1)
   // __syncthreads below orders these writes before the P/dS warps' own).
   if (DET) bwd_block_partials<BF16>(a, unit, seq_start, n0, L, false);
 
+  volatile int* skip_flag = abort_flag + 1;
   if (threadIdx.x == 0) {
+    // The device status word, read while the barriers are set up (one load per block; its
+    // latency overlaps the set-up instead of preceding it).
+    const unsigned int st0 = *reinterpret_cast<const volatile unsigned int*>(a.status);
     mbar_init(bar(BB_KV), 1);
     for (int s = 0; s < C::STAGES; ++s) {
       mbar_init(bar(BB_QF + s), 33);
@@ -345,7 +350,8 @@ __global__ void __launch_bounds__(512, 1)
     mbar_init(bar(BB_DQF), 1);
     mbar_init(bar(BB_KVD), 1);
     mbar_init(bar(BB_END), 1);
-    *abort_flag = 0;
+    *abort_flag = st0 != 0 ? 1 : 0;  // an earlier timeout: skip the work, outputs NaN
+    *skip_flag = st0 != 0 ? 1 : 0;
     fence_mbar_init();
   }
   if (warp == C::WARP_PRODUCER) {
@@ -358,7 +364,9 @@ __global__ void __launch_bounds__(512, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp >= 12) {
+  if (*skip_flag) {
+    // an earlier launch recorded a device timeout: no work (the epilogue below writes NaN)
+  } else if (warp >= 12) {
    regs_dec<C::REGS_CTRL>();
    if (warp == C::WARP_PRODUCER) {
     // ---------------------------------------------------------------- producer (whole warp)
@@ -848,9 +856,9 @@ __global__ void __launch_bounds__(256) dq_convert_kernel(Problem p, const float*
                                                          int64_t dq_rows, TensorRef dq,
                                                          DndbArgs r) {
   griddep_wait();  // launched programmatically behind the backward kernel
-  // After a device timeout (this backward's or an earlier launch's) dq, dn and db are NaN.
-  const bool failed = block_status_failed(r.status);
+  // After a device timeout (this backward's or an earlier launch's) dq, dk, dv, dn and db are NaN.
   if ((int)blockIdx.y < r.rows) {
+    const bool failed = block_status_failed(r.status);
     __shared__ double red[256];
     const int nred = (p.n_per_head ? p.Hq : 1) + 1;
     const int h = (int)blockIdx.y * (int)gridDim.x + (int)blockIdx.x;
@@ -865,6 +873,7 @@ __global__ void __launch_bounds__(256) dq_convert_kernel(Problem p, const float*
   constexpr int TPR = D / 8, RPB = 256 / TPR;
   const int zh = (int)blockIdx.y - r.rows;
   if (zh >= p.B * p.Hq) {  // dK / dV rows: sum the q-head slices' partials in order
+    const bool failed = block_status_failed(r.status);
     const int u = zh - p.B * p.Hq;
     const int z = u / (2 * p.Hkv), hkv = (u / 2) % p.Hkv, h = u & 1;
     int seq_start, L;
@@ -901,11 +910,22 @@ __global__ void __launch_bounds__(256) dq_convert_kernel(Problem p, const float*
   seq_bounds(p, z, seq_start, L);
   const int row = blockIdx.x * RPB + threadIdx.x / TPR;
   const int d0 = (threadIdx.x % TPR) * 8;
-  if (row >= L) return;
-  const int64_t src_row = p.cu_seqlens ? (int64_t)hq * dq_rows + seq_start + row
-                                       : ((int64_t)z * p.Hq + hq) * dq_rows + row;
-  const float4* s = reinterpret_cast<const float4*>(dq_accum + src_row * D + d0);
-  const float4 a0 = s[0], a1 = s[1];
+  const bool valid = row < L;
+  float4 a0 = make_float4(0.f, 0.f, 0.f, 0.f), a1 = a0;
+  if (valid) {
+    const int64_t src_row = p.cu_seqlens ? (int64_t)hq * dq_rows + seq_start + row
+                                         : ((int64_t)z * p.Hq + hq) * dq_rows + row;
+    const float4* s = reinterpret_cast<const float4*>(dq_accum + src_row * D + d0);
+    a0 = s[0];
+    a1 = s[1];
+  }
+  // The status word, read by one thread after the data loads are in flight, so its latency
+  // overlaps theirs.
+  __shared__ unsigned int s_fail;
+  if (threadIdx.x == 0) s_fail = *reinterpret_cast<const volatile unsigned int*>(r.status);
+  __syncthreads();
+  const bool failed = s_fail != 0;
+  if (!valid) return;
   T* d = reinterpret_cast<T*>(dq.ptr) + row_offset(dq, p, z, hq, seq_start, row) + d0;
   uint4 w;
   if (failed) {
@@ -1046,10 +1066,11 @@ __global__ void __launch_bounds__(512, 1)
   int seq_start, L;
   seq_bounds(p, z, seq_start, L);
   const int n0 = kvb * C::BN;
-  // Block-uniform exits: a block past the sequence end has nothing to add; after a device
-  // timeout recorded by an earlier launch, this block's outputs are NaN.
-  if (n0 >= L || block_status_failed(a.status)) {
-    bwd_block_partials<BF16>(a, unit, seq_start, n0, L, n0 < L);
+  // Block-uniform exit: a block past the sequence end has nothing to add. (A device timeout
+  // recorded by an earlier launch is checked during the set-up below: the block then skips its
+  // work and writes NaN.)
+  if (n0 >= L) {
+    bwd_block_partials<BF16>(a, unit, seq_start, n0, L, false);
     return;
   }
   const int q_start = p.causal ? n0 : 0;
@@ -1060,7 +1081,10 @@ __global__ void __launch_bounds__(512, 1)
   // every partial of this block at zero; the __syncthreads below orders these writes first.
   bwd_block_partials<BF16>(a, unit, seq_start, n0, L, false);
 
+  volatile int* skip_flag = abort_flag + 1;
   if (threadIdx.x == 0) {
+    // The device status word, read while the barriers are set up (see the D = 64 kernel).
+    const unsigned int st0 = *reinterpret_cast<const volatile unsigned int*>(a.status);
     mbar_init(bar(B2_KV), 1);
     for (int s2 = 0; s2 < C::STAGES; ++s2) {
       mbar_init(bar(B2_QF + s2), 33);
@@ -1077,7 +1101,8 @@ __global__ void __launch_bounds__(512, 1)
     mbar_init(bar(B2_DQE), 128);
     mbar_init(bar(B2_KVD), 1);
     mbar_init(bar(B2_END), 1);
-    *abort_flag = 0;
+    *abort_flag = st0 != 0 ? 1 : 0;  // an earlier timeout: skip the work, outputs NaN
+    *skip_flag = st0 != 0 ? 1 : 0;
     fence_mbar_init();
   }
   if (warp == C::WARP_PRODUCER) {
@@ -1090,7 +1115,9 @@ __global__ void __launch_bounds__(512, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp >= 12) {
+  if (*skip_flag) {
+    // an earlier launch recorded a device timeout: no work (the epilogue below writes NaN)
+  } else if (warp >= 12) {
     regs_dec<C::REGS_CTRL>();
     if (warp == C::WARP_PRODUCER) {
       // ------------------------------------------------------------ producer (whole warp)

@@ -679,10 +679,13 @@ def main():
     e1.record(st)
     barrier()
     e2e_ms = e0.elapsed_time(e1) / e2e_steps
+    e2e_per_rank = [e2e_ms]
     if world > 1:
-        t = torch.tensor([e2e_ms], device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        e2e_ms = float(t.item())
+        t = torch.zeros(world, device=dev)
+        t[rank] = e2e_ms
+        dist.all_reduce(t)  # every rank's time (each slot written by one rank)
+        e2e_per_rank = [float(x) for x in t.tolist()]
+        e2e_ms = max(e2e_per_rank)
     e2e_val = job_flops / (e2e_ms * 1e-3) / 1e12
 
     status = _lib.load().ssa_device_status(_lib.stream_ptr(dev))
@@ -718,7 +721,8 @@ def main():
             "fwd_ms": t_fwd, "bwd_ms": t_bwd,
             "frac_of_peak": value / world / peak_tf,
             "e2e": {"value": e2e_val, "unit": UNIT, "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
+                    "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
+                    "ms_per_step_per_rank": e2e_per_rank},
             "roofline": {"bound": "tensor", "kernel": "ssa_attn_bwd call (dominant)",
                          "achieved": achieved, "peak": peak_tf, "unit": "TFLOP/s",
                          "frac": achieved / peak_tf, "peak_kind": f"{peak_kind} bf16 burst",

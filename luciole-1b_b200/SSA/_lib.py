@@ -6,6 +6,7 @@ raises. There is no CPU or PyTorch fallback.
 
 from __future__ import annotations
 
+import contextlib
 import ctypes
 import os
 import threading
@@ -133,8 +134,56 @@ def tensor_thd(t: torch.Tensor) -> SsaTensor:
     return SsaTensor(t.data_ptr(), 0, t.stride(1), t.stride(0))
 
 
+_raw_stream = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+
+
 def stream_ptr(device: torch.device) -> ctypes.c_void_p:
+    """The current CUDA stream of `device` as a cudaStream_t (read without building a Stream
+    object: this runs on every attention call)."""
+    if _raw_stream is not None:
+        idx = device.index if device.index is not None else torch.cuda.current_device()
+        return ctypes.c_void_p(_raw_stream(idx))
     return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def device_guard(device: torch.device):
+    """Makes `device` current for the duration of a call, and restores the caller's device after
+    (the C entry points make the tensors' device current). A no-op when it already is."""
+    if device.index is None or device.index == torch.cuda.current_device():
+        return contextlib.nullcontext()
+    return torch.cuda.device(device)
+
+
+_family_cache: dict = {}
+_ws_cache: dict = {}
+
+
+def kernel_family_of(prob: "SsaProblem") -> int:
+    """ssa_attn_kernel_family for a validated problem; the answer depends only on the dtype, the
+    head dim and the sign of the softmax scale, so it is asked once per combination."""
+    key = (prob.dtype, prob.D, prob.softmax_scale > 0)
+    fam = _family_cache.get(key)
+    if fam is None:
+        fam = load().ssa_attn_kernel_family(ctypes.byref(prob))
+        if fam >= 0:
+            _family_cache[key] = fam
+    return fam
+
+
+def bwd_workspace_size(prob: "SsaProblem") -> int:
+    """ssa_attn_bwd_workspace_size, asked once per problem shape (the size depends on the shape,
+    dtype, causality, head dim, per-head n, packing, the deterministic flag and the q-head-slice
+    override SSA_BWD_HSPLIT, not on pointers)."""
+    key = (prob.dtype, prob.B, prob.Hq, prob.Hkv, prob.N, prob.D, prob.causal,
+           prob.softmax_scale > 0, prob.n_per_head, bool(prob.cu_seqlens), prob.max_seqlen,
+           prob.deterministic, os.environ.get("SSA_BWD_HSPLIT"))
+    ws = _ws_cache.get(key)
+    if ws is None:
+        ws = int(load().ssa_attn_bwd_workspace_size(ctypes.byref(prob)))
+        if len(_ws_cache) > 4096:
+            _ws_cache.clear()
+        _ws_cache[key] = ws
+    return ws
 
 
 def launch_count() -> int:

@@ -33,9 +33,16 @@ __all__ = [
 ]
 
 
+def _as_f32(x, device) -> torch.Tensor:
+    if (isinstance(x, torch.Tensor) and x.dtype == torch.float32 and x.device == device
+            and x.is_contiguous()):
+        return x.detach()
+    return torch.as_tensor(x).detach().to(device=device, dtype=torch.float32).contiguous()
+
+
 def _params(ssa_n: torch.Tensor, ssa_b: torch.Tensor, hq: int, device) -> Tuple[torch.Tensor, torch.Tensor, int]:
-    n = torch.as_tensor(ssa_n).detach().to(device=device, dtype=torch.float32).contiguous()
-    b = torch.as_tensor(ssa_b).detach().to(device=device, dtype=torch.float32).contiguous()
+    n = _as_f32(ssa_n, device)
+    b = _as_f32(ssa_b, device)
     if b.numel() != 1:
         raise ValueError(f"ssa_b must be a scalar tensor, got shape {tuple(b.shape)}")
     if n.numel() == 1:
@@ -130,13 +137,13 @@ def ssa_flash_attn_forward(q, k, v, softmax_scale, ssa_n, ssa_b, causal=True):
     B, Hq, Hkv, N, D = _check_qkv(q, k, v)
     n, b, per_head = _params(ssa_n, ssa_b, Hq, q.device)
     prob = _problem(q, Hkv, softmax_scale, n, b, per_head, causal, B, N)
-    fam = lib.ssa_attn_kernel_family(ctypes.byref(prob))
+    fam = _lib.kernel_family_of(prob)
     q, k, v = _prep(q, fam), _prep(k, fam), _prep(v, fam)
     out = torch.empty_like(q)
     if fam == 1 and not _tma_ok(out):
         out = torch.empty(q.shape, dtype=q.dtype, device=q.device)
     m = torch.empty((B, Hq, N), device=q.device, dtype=torch.float32)
-    with torch.cuda.device(q.device):
+    with _lib.device_guard(q.device):
         rc = lib.ssa_attn_fwd(ctypes.byref(prob), _lib.tensor_bhnd(q), _lib.tensor_bhnd(k),
                               _lib.tensor_bhnd(v), _lib.tensor_bhnd(out), m.data_ptr(), None, 0,
                               _lib.stream_ptr(q.device))
@@ -170,14 +177,14 @@ def ssa_flash_attn_backward(q, k, v, out, dout, m, softmax_scale, ssa_n, ssa_b, 
     n, b, per_head = _params(ssa_n, ssa_b, Hq, q.device)
     det = _lib.deterministic_default() if deterministic is None else bool(deterministic)
     prob = _problem(q, Hkv, softmax_scale, n, b, per_head, causal, B, N, deterministic=det)
-    fam = lib.ssa_attn_kernel_family(ctypes.byref(prob))
+    fam = _lib.kernel_family_of(prob)
     q, k, v, dout = _prep(q, fam), _prep(k, fam), _prep(v, fam), _prep(dout, fam)
     out = _prep(out, fam)
     dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
     dn, db = _param_grad_pair(n, q.device)
-    ws_bytes = lib.ssa_attn_bwd_workspace_size(ctypes.byref(prob))
+    ws_bytes = _lib.bwd_workspace_size(prob)
     ws = torch.empty(max(ws_bytes, 1), device=q.device, dtype=torch.uint8)
-    with torch.cuda.device(q.device):
+    with _lib.device_guard(q.device):
         rc = lib.ssa_attn_bwd(ctypes.byref(prob), _lib.tensor_bhnd(q), _lib.tensor_bhnd(k),
                               _lib.tensor_bhnd(v), _lib.tensor_bhnd(out), _lib.tensor_bhnd(dout),
                               m.data_ptr(), _lib.tensor_bhnd(dq), _lib.tensor_bhnd(dk),
@@ -230,12 +237,12 @@ def ssa_flash_attn_varlen_forward(q, k, v, cu_seqlens, max_seqlen, softmax_scale
     n, b, per_head = _params(ssa_n, ssa_b, Hq, q.device)
     prob = _problem(q, Hkv, softmax_scale, n, b, per_head, causal, ndoc, T,
                     cu_seqlens, max_seqlen, cu_pad)
-    fam = lib.ssa_attn_kernel_family(ctypes.byref(prob))
+    fam = _lib.kernel_family_of(prob)
     q, k, v = _prep(q, fam), _prep(k, fam), _prep(v, fam)
     alloc = torch.zeros if cu_pad is not None else torch.empty
     out = alloc(q.shape, dtype=q.dtype, device=q.device)
     lse = torch.empty((Hq, T), device=q.device, dtype=torch.float32)
-    with torch.cuda.device(q.device):
+    with _lib.device_guard(q.device):
         rc = lib.ssa_attn_fwd(ctypes.byref(prob), _lib.tensor_thd(q), _lib.tensor_thd(k),
                               _lib.tensor_thd(v), _lib.tensor_thd(out), lse.data_ptr(), None, 0,
                               _lib.stream_ptr(q.device))
@@ -256,7 +263,7 @@ def ssa_flash_attn_varlen_backward(q, k, v, out, dout, lse, cu_seqlens, max_seql
     det = _lib.deterministic_default() if deterministic is None else bool(deterministic)
     prob = _problem(q, Hkv, softmax_scale, n, b, per_head, causal, ndoc, T,
                     cu_seqlens, max_seqlen, cu_pad, deterministic=det)
-    fam = lib.ssa_attn_kernel_family(ctypes.byref(prob))
+    fam = _lib.kernel_family_of(prob)
     q, k, v, dout = _prep(q, fam), _prep(k, fam), _prep(v, fam), _prep(dout, fam)
     out = _prep(out, fam)
     alloc = torch.zeros if cu_pad is not None else torch.empty
@@ -264,9 +271,9 @@ def ssa_flash_attn_varlen_backward(q, k, v, out, dout, lse, cu_seqlens, max_seql
     dk = alloc(k.shape, dtype=k.dtype, device=k.device)
     dv = alloc(v.shape, dtype=v.dtype, device=v.device)
     dn, db = _param_grad_pair(n, q.device)
-    ws_bytes = lib.ssa_attn_bwd_workspace_size(ctypes.byref(prob))
+    ws_bytes = _lib.bwd_workspace_size(prob)
     ws = torch.empty(max(ws_bytes, 1), device=q.device, dtype=torch.uint8)
-    with torch.cuda.device(q.device):
+    with _lib.device_guard(q.device):
         rc = lib.ssa_attn_bwd(ctypes.byref(prob), _lib.tensor_thd(q), _lib.tensor_thd(k),
                               _lib.tensor_thd(v), _lib.tensor_thd(out), _lib.tensor_thd(dout),
                               lse.data_ptr(), _lib.tensor_thd(dq), _lib.tensor_thd(dk),

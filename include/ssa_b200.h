@@ -120,7 +120,8 @@ int ssa_attn_bwd_noalloc(const ssa_problem_t* prob,
                          float* dn, float* db, void* stream);
 
 /* Which kernel family serves this problem: 0 = generic (fp32-compute SIMT: fp32 inputs or
- * head dims without a tensor-core kernel), 1 = sm_100a tcgen05/TMA kernels. */
+ * D = 16, which has no tensor-core kernel), 1 = sm_100a tcgen05/TMA kernels (bf16/fp16 with
+ * D in {32, 64, 128}; D = 32 runs the D = 64 kernels). */
 int ssa_attn_kernel_family(const ssa_problem_t* prob);
 
 /* Reads and clears the device status word written by bounded device-side waits

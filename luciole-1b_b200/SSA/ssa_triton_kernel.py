@@ -3,7 +3,7 @@
 Drop-in for the reference module ``SSA.ssa_triton_kernel``
 (training/train/train_ssa_triton/SSA/ssa_triton_kernel.py): same function names, argument
 meaning and return values, computed by hand-written sm_100a CUDA (tcgen05/TMA for bf16/fp16
-with D in {64, 128}; fp32-arithmetic CUDA-core kernels for fp32 and other head dims). The
+with D in {32, 64, 128}; fp32-arithmetic CUDA-core kernels for fp32 and D = 16). The
 module name is kept so ``from SSA.ssa_triton_kernel import ...`` keeps working; nothing here
 uses Triton.
 

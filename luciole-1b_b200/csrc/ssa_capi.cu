@@ -89,7 +89,8 @@ Problem to_problem(const ssa_problem_t* pr) {
 
 TensorRef to_ref(const ssa_tensor_t& t) { return TensorRef{t.ptr, t.sB, t.sH, t.sN}; }
 
-// Tensor-core family: 16-bit inputs, D in {64, 128}, positive scale, TMA-legal layouts.
+// Tensor-core family: 16-bit inputs, D in {32, 64, 128} (32 on the D = 64 kernels), positive
+// scale, TMA-legal layouts.
 bool use_sm100(const ssa_problem_t* pr) {
   return sm100_supports(pr->dtype, pr->D) && pr->softmax_scale > 0.f;
 }

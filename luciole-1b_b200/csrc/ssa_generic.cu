@@ -2,8 +2,8 @@
 //
 // These serve fp32 inputs (the reference's fp32 mode, ssa_triton_kernel.py:779-784, where the
 // parity bar is 1e-5 relative and tensor cores cannot help: tcgen05 has no full-fp32 MMA) and
-// head dims that have no tcgen05 kernel (D in {16, 32}; the reference's own test matrix uses
-// D = 32, check_ssa_triton_parity.py:1025). bf16/fp16 with D in {64, 128} run on the sm_100a
+// the head dim that has no tcgen05 kernel (D = 16). bf16/fp16 with D in {32, 64, 128} (the
+// reference's own test matrix uses D = 32, check_ssa_triton_parity.py:1025) run on the sm_100a
 // tcgen05 kernels instead (ssa_sm100_fwd.cu / ssa_sm100_bwd.cu).
 //
 // Structure follows the reference's kernel set:

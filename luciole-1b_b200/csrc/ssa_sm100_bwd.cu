@@ -171,7 +171,7 @@ __device__ __forceinline__ void store_dkv_row(const BwdArgs& a, const BwdUnit& u
         for (int i = 0; i < 8; ++i)
           d4[i] = make_float4(__uint_as_float(o[4 * i]), __uint_as_float(o[4 * i + 1]),
                               __uint_as_float(o[4 * i + 2]), __uint_as_float(o[4 * i + 3]));
-      } else {
+      } else if (c * 32 < p.D) {  // p.D < D when a D = 32 problem runs the D = 64 kernel
         uint32_t w[16];
 #pragma unroll
         for (int i = 0; i < 16; ++i)
@@ -775,8 +775,10 @@ __global__ void __launch_bounds__(512, 1)
 // Backward preprocess for the tensor-core path, one pass: delta = rowsum(O * dO) in fp32
 // (ssa_triton_kernel.py:267-298) and zeroing of the fp32 dQ accumulator rows (padding rows
 // included) and, for deterministic dq, of the turn counters (sem_per_zh per sequence x q-head).
-// D/8 threads per row, 16-byte loads; 2048/D rows per 256-thread block.
-template <typename T, int D>
+// D/8 threads per row (D: the tensors' head dim), 16-byte loads; 2048/D rows per 256-thread block.
+// The accumulator rows are DACC floats wide (the kernel's head dim: 64 when D = 32 runs the D = 64
+// kernel).
+template <typename T, int D, int DACC>
 __global__ void __launch_bounds__(256) bwd_preprocess_sm100_kernel(Problem p, TensorRef o,
                                                                    TensorRef dout, float* delta,
                                                                    float* dq_accum,
@@ -792,9 +794,10 @@ __global__ void __launch_bounds__(256) bwd_preprocess_sm100_kernel(Problem p, Te
     }
   }
   constexpr int TPR = D / 8, RPB = 256 / TPR;
+  constexpr int ZPT = DACC / TPR;  // accumulator floats zeroed per thread
   const int sub = threadIdx.x % TPR;
   const int rr = blockIdx.x * RPB + threadIdx.x / TPR;  // row within the head's accumulator
-  if (rr >= dq_rows) return;
+  const bool in_acc = rr < dq_rows;  // (no early return: every lane takes part in the shuffles)
   int z, hq, row, L;
   if (p.cu_seqlens) {  // accumulator rows are packed tokens; delta is [Hq][T]
     z = 0;
@@ -807,12 +810,14 @@ __global__ void __launch_bounds__(256) bwd_preprocess_sm100_kernel(Problem p, Te
     row = rr;
     L = p.N;
   }
-  float4* zdst = reinterpret_cast<float4*>(
-      dq_accum + ((int64_t)blockIdx.y * dq_rows + rr) * D + sub * 8);
-  zdst[0] = make_float4(0.f, 0.f, 0.f, 0.f);
-  zdst[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+  if (in_acc) {
+    float4* zdst = reinterpret_cast<float4*>(
+        dq_accum + ((int64_t)blockIdx.y * dq_rows + rr) * DACC + sub * ZPT);
+#pragma unroll
+    for (int i = 0; i < ZPT / 4; ++i) zdst[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
   float acc = 0.f;
-  const bool valid = row < L;
+  const bool valid = in_acc && row < L;
   if (valid) {
     const int64_t oo = (p.cu_seqlens ? 0 : (int64_t)z * o.sB) + (int64_t)hq * o.sH + (int64_t)row * o.sN;
     const int64_t od = (p.cu_seqlens ? 0 : (int64_t)z * dout.sB) + (int64_t)hq * dout.sH +
@@ -851,7 +856,8 @@ struct DndbArgs {
   TensorRef dk, dv;
 };
 
-template <typename T, int D>
+// D: the tensors' head dim (the columns written); DACC: the accumulator's row width.
+template <typename T, int D, int DACC>
 __global__ void __launch_bounds__(256) dq_convert_kernel(Problem p, const float* dq_accum,
                                                          int64_t dq_rows, TensorRef dq,
                                                          DndbArgs r) {
@@ -890,11 +896,11 @@ __global__ void __launch_bounds__(256) dq_convert_kernel(Problem p, const float*
     }
     const int kvb = row >> 7;
     const float* src = r.dkv_part +
-                       ((((int64_t)z * p.Hkv + hkv) * r.nkv + kvb) * r.hsplit * 2 + h) * (128 * D) +
-                       (int64_t)(row & 127) * D + d0;
+                       ((((int64_t)z * p.Hkv + hkv) * r.nkv + kvb) * r.hsplit * 2 + h) * (128 * DACC) +
+                       (int64_t)(row & 127) * DACC + d0;
     float4 a0 = make_float4(0.f, 0.f, 0.f, 0.f), a1 = a0;
     for (int sp = 0; sp < r.hsplit; ++sp) {
-      const float4* s4 = reinterpret_cast<const float4*>(src + (int64_t)sp * 2 * 128 * D);
+      const float4* s4 = reinterpret_cast<const float4*>(src + (int64_t)sp * 2 * 128 * DACC);
       const float4 b0 = s4[0], b1 = s4[1];
       a0 = make_float4(a0.x + b0.x, a0.y + b0.y, a0.z + b0.z, a0.w + b0.w);
       a1 = make_float4(a1.x + b1.x, a1.y + b1.y, a1.z + b1.z, a1.w + b1.w);
@@ -915,7 +921,7 @@ __global__ void __launch_bounds__(256) dq_convert_kernel(Problem p, const float*
   if (valid) {
     const int64_t src_row = p.cu_seqlens ? (int64_t)hq * dq_rows + seq_start + row
                                          : ((int64_t)z * p.Hq + hq) * dq_rows + row;
-    const float4* s = reinterpret_cast<const float4*>(dq_accum + src_row * D + d0);
+    const float4* s = reinterpret_cast<const float4*>(dq_accum + src_row * DACC + d0);
     a0 = s[0];
     a1 = s[1];
   }
@@ -962,7 +968,7 @@ cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t sme
 }
 
 // dq conversion + dn / db reduction, one launch.
-template <typename T, int D>
+template <typename T, int D, int DACC>
 int launch_dq_convert_dndb(const Problem& p, const float* dq_accum, int64_t dq_rows,
                             TensorRef dq, const float* dn_part, const float* db_part, int P,
                             float* dn, float* db, const BwdArgs& a, cudaStream_t st) {
@@ -972,7 +978,7 @@ int launch_dq_convert_dndb(const Problem& p, const float* dq_accum, int64_t dq_r
   const int extra_rows = (nred + gx - 1) / gx;
   const int dkv_rows = a.hsplit > 1 ? p.B * p.Hkv * 2 : 0;
   dim3 gc((unsigned)gx, (unsigned)(p.B * p.Hq + extra_rows + dkv_rows));
-  if (launch_pdl(dq_convert_kernel<T, D>, gc, dim3(256), 0, st, p, dq_accum, dq_rows, dq,
+  if (launch_pdl(dq_convert_kernel<T, D, DACC>, gc, dim3(256), 0, st, p, dq_accum, dq_rows, dq,
                  DndbArgs{dn_part, db_part, P, extra_rows, dn, db, device_status_ptr(),
                           a.dkv_part, a.hsplit, a.nkv, a.dk, a.dv}) != cudaSuccess)
     return SSA_ERR_LAUNCH;
@@ -1531,12 +1537,13 @@ inline size_t al256(size_t x) { return (x + 255) & ~static_cast<size_t>(255); }
 BwdLayout bwd_layout(const Problem& p) {
   BwdLayout l;
   l.nkv = (p.max_seqlen + 127) / 128;
+  const int dk = p.D == 128 ? 128 : 64;  // the kernel's head dim (D = 32 runs the D = 64 kernel)
   if (p.cu_seqlens) {
     l.dq_rows = (int64_t)p.N + 128;
-    l.dq_bytes = al256(sizeof(float) * (size_t)p.Hq * l.dq_rows * p.D);
+    l.dq_bytes = al256(sizeof(float) * (size_t)p.Hq * l.dq_rows * dk);
   } else {
     l.dq_rows = (int64_t)((p.N + 127) / 128) * 128;
-    l.dq_bytes = al256(sizeof(float) * (size_t)p.B * p.Hq * l.dq_rows * p.D);
+    l.dq_bytes = al256(sizeof(float) * (size_t)p.B * p.Hq * l.dq_rows * dk);
   }
   const int bt = p.D == 128 ? 64 : 128;  // query tile rows of the kernel
   l.ntq = (p.max_seqlen + bt - 1) / bt;
@@ -1545,7 +1552,7 @@ BwdLayout bwd_layout(const Problem& p) {
   l.sem_bytes = p.det ? al256(sizeof(int) * (size_t)p.B * p.Hq * l.ntq * 4) : 0;
   l.hsplit = choose_hsplit(p, bt);
   l.dkv_bytes = l.hsplit > 1 ? al256(sizeof(float) * (size_t)p.B * p.Hkv * l.nkv * l.hsplit * 2 *
-                                     128 * p.D)
+                                     128 * dk)
                              : 0;
   l.total = l.dq_bytes + 2 * l.part_bytes + l.dkv_bytes + l.sem_bytes;
   return l;
@@ -1588,9 +1595,15 @@ int run_bwd(const Problem& p, TensorRef q, TensorRef k, TensorRef v, TensorRef o
                    : nullptr;
   {
     using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
-    dim3 gp((unsigned)((lay.dq_rows + 31) / 32), p.cu_seqlens ? p.Hq : p.B * p.Hq);
-    bwd_preprocess_sm100_kernel<T, 64><<<gp, 256, 0, st>>>(p, out, dout, delta, a.dq_accum,
-                                                            lay.dq_rows, a.dq_sem, 4 * lay.ntq);
+    const unsigned gy = p.cu_seqlens ? p.Hq : p.B * p.Hq;
+    if (p.D == 32)
+      bwd_preprocess_sm100_kernel<T, 32, 64>
+          <<<dim3((unsigned)((lay.dq_rows + 63) / 64), gy), 256, 0, st>>>(
+              p, out, dout, delta, a.dq_accum, lay.dq_rows, a.dq_sem, 4 * lay.ntq);
+    else
+      bwd_preprocess_sm100_kernel<T, 64, 64>
+          <<<dim3((unsigned)((lay.dq_rows + 31) / 32), gy), 256, 0, st>>>(
+              p, out, dout, delta, a.dq_accum, lay.dq_rows, a.dq_sem, 4 * lay.ntq);
     note_launches(1);
   }
   // dQ accumulator as a 2-D fp32 tensor [rows][64] for the drain's tiled reduce-adds:
@@ -1618,8 +1631,11 @@ int run_bwd(const Problem& p, TensorRef q, TensorRef k, TensorRef v, TensorRef o
     return SSA_ERR_LAUNCH;
   note_launches(1);
   using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
-  return launch_dq_convert_dndb<T, 64>(p, a.dq_accum, a.dq_rows, dq, a.dn_part, a.db_part,
-                                       lay.ppk * lay.nkv, dn, db, a, st);
+  if (p.D == 32)
+    return launch_dq_convert_dndb<T, 32, 64>(p, a.dq_accum, a.dq_rows, dq, a.dn_part, a.db_part,
+                                             lay.ppk * lay.nkv, dn, db, a, st);
+  return launch_dq_convert_dndb<T, 64, 64>(p, a.dq_accum, a.dq_rows, dq, a.dn_part, a.db_part,
+                                           lay.ppk * lay.nkv, dn, db, a, st);
 }
 
 template <bool BF16>
@@ -1660,7 +1676,7 @@ int run_bwd128(const Problem& p, TensorRef q, TensorRef k, TensorRef v, TensorRe
                    : nullptr;
   {
     dim3 gp((unsigned)((lay.dq_rows + 15) / 16), p.cu_seqlens ? p.Hq : p.B * p.Hq);
-    bwd_preprocess_sm100_kernel<T, 128><<<gp, 256, 0, st>>>(p, out, dout, delta, a.dq_accum,
+    bwd_preprocess_sm100_kernel<T, 128, 128><<<gp, 256, 0, st>>>(p, out, dout, delta, a.dq_accum,
                                                              lay.dq_rows, a.dq_sem, 4 * lay.ntq);
   }
   {  // dQ accumulator as 2-D fp32 [rows][128]; {32 head dims x 64 queries} boxes, no swizzle
@@ -1682,14 +1698,14 @@ int run_bwd128(const Problem& p, TensorRef q, TensorRef k, TensorRef v, TensorRe
   const long long grid = (long long)lay.nkv * p.B * p.Hkv * lay.hsplit;
   kern<<<(unsigned)grid, C::THREADS, C::SMEM_BYTES, st>>>(tq, tk, tv, tdo, tdq, a);
   note_launches(2);
-  return launch_dq_convert_dndb<T, 128>(p, a.dq_accum, a.dq_rows, dq, a.dn_part, a.db_part,
+  return launch_dq_convert_dndb<T, 128, 128>(p, a.dq_accum, a.dq_rows, dq, a.dn_part, a.db_part,
                                         lay.ppk * lay.nkv, dn, db, a, st);
 }
 
 }  // namespace sm100
 
-bool sm100_bwd_supports(int dtype, int D) {
-  return (dtype == SSA_DTYPE_BF16 || dtype == SSA_DTYPE_F16) && (D == 64 || D == 128);
+bool sm100_bwd_supports(int dtype, int D) {  // D = 32 runs the D = 64 kernel (see sm100_supports)
+  return (dtype == SSA_DTYPE_BF16 || dtype == SSA_DTYPE_F16) && (D == 32 || D == 64 || D == 128);
 }
 
 size_t sm100_bwd_workspace_bytes(const Problem& p) { return sm100::bwd_layout(p).total; }
@@ -1704,7 +1720,7 @@ int launch_bwd_sm100(int dtype, const Problem& p, TensorRef q, TensorRef k, Tens
                                          ws, ws_bytes, st)
                : sm100::run_bwd128<false>(p, q, k, v, out, dout, lse, delta, dq, dk, dv, dn, db,
                                           ws, ws_bytes, st);
-  if (p.D != 64) return SSA_ERR_UNSUPPORTED;
+  if (p.D != 64 && p.D != 32) return SSA_ERR_UNSUPPORTED;
   return dtype == SSA_DTYPE_BF16
              ? sm100::run_bwd<true>(p, q, k, v, out, dout, lse, delta, dq, dk, dv, dn, db, ws,
                                     ws_bytes, st)

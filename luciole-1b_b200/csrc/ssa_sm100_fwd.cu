@@ -409,7 +409,9 @@ __global__ void __launch_bounds__(192, 2)
         uint32_t o[32];
         tmem_ld32(t_lane + C::COL_O + c * 32, o);
         tmem_ld_wait(o);
-        if (row < L) {
+        // p.D is the tensors' head dim: 32 when a D = 32 problem runs this D = 64 kernel (its
+        // TMA boxes zero-fill columns 32..63, so those O columns are zero and not stored).
+        if (row < L && c * 32 < p.D) {
           uint32_t w[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i)
@@ -485,15 +487,20 @@ int launch_selftest_timeout(unsigned int* status, long long cycles, cudaStream_t
   return SSA_OK;
 }
 
+// Head dims with a tensor-core kernel. D = 32 runs the D = 64 kernels: their TMA boxes are 64
+// elements wide, so a D = 32 tensor's boxes read zeros in columns 32..63 (out-of-bounds fill),
+// which add nothing to S, O, dQ, dK or dV; the epilogues store the first p.D columns only. The
+// MMAs then do twice the needed work, but at D = 64 the special-function work per score element,
+// not the tensor pipe, bounds these kernels.
 bool sm100_supports(int dtype, int D) {
-  return (dtype == SSA_DTYPE_BF16 || dtype == SSA_DTYPE_F16) && (D == 64 || D == 128);
+  return (dtype == SSA_DTYPE_BF16 || dtype == SSA_DTYPE_F16) && (D == 32 || D == 64 || D == 128);
 }
 
 int launch_fwd_sm100(int dtype, const Problem& p, TensorRef q, TensorRef k, TensorRef v,
                      TensorRef o, float* lse, cudaStream_t st) {
   const bool bf = dtype == SSA_DTYPE_BF16;
-  if (p.D == 64) return bf ? sm100::run_fwd<64, true>(p, q, k, v, o, lse, st)
-                           : sm100::run_fwd<64, false>(p, q, k, v, o, lse, st);
+  if (p.D == 64 || p.D == 32) return bf ? sm100::run_fwd<64, true>(p, q, k, v, o, lse, st)
+                                         : sm100::run_fwd<64, false>(p, q, k, v, o, lse, st);
   if (p.D == 128) return bf ? sm100::run_fwd<128, true>(p, q, k, v, o, lse, st)
                             : sm100::run_fwd<128, false>(p, q, k, v, o, lse, st);
   return SSA_ERR_UNSUPPORTED;

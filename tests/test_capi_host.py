@@ -60,7 +60,8 @@ def test_family_selection(lib):
     assert lib.ssa_attn_kernel_family(ctypes.byref(_prob())) == 1          # bf16 D=64
     assert lib.ssa_attn_kernel_family(ctypes.byref(_prob(dtype=1, D=128))) == 1
     assert lib.ssa_attn_kernel_family(ctypes.byref(_prob(dtype=0))) == 0   # fp32 -> generic
-    assert lib.ssa_attn_kernel_family(ctypes.byref(_prob(D=32))) == 0      # D=32 -> generic
+    assert lib.ssa_attn_kernel_family(ctypes.byref(_prob(D=32))) == 1      # D=32: the D=64 kernels
+    assert lib.ssa_attn_kernel_family(ctypes.byref(_prob(D=16))) == 0      # D=16 -> generic
     assert lib.ssa_attn_kernel_family(ctypes.byref(_prob(softmax_scale=-1.0))) == 0
     assert lib.ssa_attn_kernel_family(ctypes.byref(_prob(Hq=6, Hkv=4))) == -1
 

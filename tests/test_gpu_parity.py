@@ -4,7 +4,7 @@ reference's golden vectors, on identical seeded inputs.
 Tolerances (written here, applied below):
   * fp32 inputs (generic kernels): max|a-r| / max|r| <= 1e-5 for out/dq/dk/dv, and
     |a-r| <= 1e-5 * |r| + 1e-6 for dn/db.
-  * bf16/fp16 inputs (tcgen05 kernels for D in {64,128}): against the fp64 oracle evaluated on
+  * bf16/fp16 inputs (tcgen05 kernels for D in {32,64,128}): against the fp64 oracle evaluated on
     the same 16-bit inputs, elementwise |a-r| <= 2e-2 + 5e-2 |r| (the reference's own bf16 rule,
     check_ssa_triton_parity.py:1059-1062) AND max-abs <= 2e-2 wherever |r| <= 4 (bf16 cannot
     represent values above 4 to within 2e-2 absolute: its spacing there is 2^-5);
@@ -97,6 +97,11 @@ CASES = [
     (2, 4, 2, 144, 64, True, torch.bfloat16, False),    # one tile + 16: a lone 16-query chunk
     (1, 4, 1, 47, 64, True, torch.bfloat16, True),      # ragged inside the first 16-query chunk
     (1, 6, 3, 144, 128, True, torch.bfloat16, True),    # D = 128, GQA 2, ragged
+    # D = 32 runs the D = 64 kernels, whose TMA boxes zero-fill columns 32..63
+    (2, 8, 2, 512, 32, True, torch.bfloat16, False),
+    (1, 4, 2, 300, 32, False, torch.float16, True),     # non-causal, ragged, fp16
+    (1, 24, 8, 256, 32, True, torch.bfloat16, True),    # 24 heads of 32 (GQA 3)
+    (2, 4, 1, 200, 32, True, torch.bfloat16, True),     # ragged, GQA 4
 ]
 
 
@@ -126,7 +131,7 @@ def test_kernel_vs_oracle(B, Hq, Hkv, N, D, causal, dtype, per_head, cuda_device
     assert_scalar_close("db", r["db"], ref["db"])
 
 
-@pytest.mark.parametrize("D", [64, 128])
+@pytest.mark.parametrize("D", [32, 64, 128])
 def test_qhead_slices_of_a_key_block(D, cuda_device, monkeypatch):
     """With few sequences the backward splits each key block's GQA q-heads over 2 or 4 CTAs
     (their fp32 dK / dV partials are summed in slice order by the dq conversion). Every split,
@@ -402,6 +407,7 @@ def test_bit_deterministic(dtype, cuda_device):
     (2, 8, 2, 1024, 64, True),     # 8 key blocks per sequence: long chains of ordered dQ adds
     (1, 8, 2, 700, 64, False),     # non-causal: every key block adds to every tile; q-head slices
     (1, 4, 2, 640, 128, True),     # D = 128 kernel (64-query tiles)
+    (2, 8, 2, 512, 32, True),      # D = 32 through the D = 64 kernel
 ])
 def test_deterministic_dq_is_bit_identical(B, Hq, Hkv, N, D, causal, cuda_device):
     """deterministic=True: every dQ tile's contributions are added in ascending key-block order,

@@ -188,7 +188,13 @@ def measured_peaks():
 
 class ClockSampler:
     """Samples SM clock and throttle reasons through NVML while the timed region runs (reads
-    only; no GPU setting is changed)."""
+    only; no GPU setting is changed).
+
+    deferred=True samples only after arm(), which the caller invokes once the host has queued
+    the whole timed region and is about to block in a synchronize: the samples then fall while
+    the device runs the queued work, and the sampling thread never competes for the interpreter
+    lock with the thread that launches the kernels (a sampler running during the launches
+    delayed them by up to 15 ms, long enough to show in a timed region of 20 steps of ~1 ms)."""
 
     REASONS = {
         0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
@@ -197,23 +203,33 @@ class ClockSampler:
         0x100: "display_clock_setting",
     }
 
-    def __init__(self, index: int):
+    def __init__(self, index: int, deferred: bool = False):
         self.samples, self.reasons, self.max_mhz = [], set(), None
-        self._stop = threading.Event()
+        self._stop, self._armed = threading.Event(), threading.Event()
+        self._interval = 0.002 if deferred else 0.02
+        if not deferred:
+            self._armed.set()
         try:
             import pynvml
             pynvml.nvmlInit()
             self._nv = pynvml
             self._h = pynvml.nvmlDeviceGetHandleByIndex(index)
             self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+            # first calls resolve the library entry points: done here, outside the timed region
+            pynvml.nvmlDeviceGetClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+            pynvml.nvmlDeviceGetCurrentClocksEventReasons(self._h)
         except Exception:
             self._nv = None
         self._t = threading.Thread(target=self._run, daemon=True)
 
+    def arm(self):
+        self._armed.set()
+
     def _run(self):
+        self._armed.wait()
         while not self._stop.is_set():
             self._sample()
-            self._stop.wait(0.02)
+            self._stop.wait(self._interval)
 
     def _sample(self):
         try:
@@ -232,6 +248,7 @@ class ClockSampler:
 
     def __exit__(self, *a):
         self._stop.set()
+        self._armed.set()
         if self._nv is not None:
             self._t.join(timeout=1)
             self._sample()  # the timed region's end
@@ -560,45 +577,57 @@ def main():
         dnb_full[HQ:].copy_(db_.reshape(1))
         return dist.all_reduce(dnb_full, async_op=async_op)
 
-    def step():
+    st = torch.cuda.current_stream(dev)
+
+    def step(pending, evs=None):
+        """One step as the timed loop runs it: the dn/db all-reduce is issued asynchronously and
+        overlaps the next step's forward (the warm-up runs the same steps, so the first
+        asynchronous collective is not inside the timed region). evs: events recorded before
+        the forward, between forward and backward, and after the backward."""
+        if evs:
+            evs[0].record(st)
         out, m = attn_fwd(q, k, v)
+        if evs:
+            evs[1].record(st)
         dq, dk, dv, dn, db = attn_bwd(q, k, v, out, do, m)
+        if evs:
+            evs[2].record(st)
         if reduce_params:
-            reduce_dn_db(dn, db)
-        return out, dq, dk, dv, dn, db
+            # in place on the (adjacent) dn/db
+            pending.append(reduce_dn_db(dn, db, async_op=True))
 
     def barrier():
         if world > 1:
             dist.barrier(device_ids=[local])
         torch.cuda.synchronize(dev)
 
+    pending = []
     for _ in range(args.warmup):
-        step()
+        step(pending)
+    for w in pending:
+        w.wait()
     barrier()
 
     # ---- value: device-resident inputs; per-call events for the roofline
-    st = torch.cuda.current_stream(dev)
     launches0 = _lib.launch_count()
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True),
            torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
     start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     pending = []
-    with ClockSampler(local) as clk:
+    with ClockSampler(local, deferred=True) as clk:
         barrier()
+        # A device-side wait of ~0.5 ms ahead of the start event lets the host queue the first
+        # steps before the device reaches them, as in a training loop's steady state; without it
+        # the first timed step also carries the host's launch latency (~0.1 ms, 4% of a 20-step
+        # region at 8 GPUs). The timed region still holds exactly the K steps.
+        torch.cuda._sleep(1_000_000)
         start.record(st)
         for i in range(args.steps):
-            e0, e1, e2 = ev[i]
-            e0.record(st)
-            out, m = attn_fwd(q, k, v)
-            e1.record(st)
-            dq, dk, dv, dn, db = attn_bwd(q, k, v, out, do, m)
-            e2.record(st)
-            if reduce_params:
-                # in place on the (adjacent) dn/db; overlaps the next step's forward
-                pending.append(reduce_dn_db(dn, db, async_op=True))
+            step(pending, ev[i])
         for w in pending:  # every reduction finishes inside the timed region
             w.wait()
         stop.record(st)
+        clk.arm()
         barrier()
     launches = _lib.launch_count() - launches0
     ms = start.elapsed_time(stop) / args.steps

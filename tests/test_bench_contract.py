@@ -95,3 +95,36 @@ def test_reference_arm_prints_one_contract_line():
     assert d["e2e"]["value"] == d["value"]
     assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["e2e"]["d2h_bytes_per_step"] == 0
     assert d["ms_per_step"] > 0 and d["sample_flops_per_step"] > 0
+
+
+def test_clock_sampler_defers_until_armed(bench, monkeypatch):
+    """A deferred sampler takes no sample while the timed region is being queued (its thread
+    would compete with the launching thread for the interpreter lock), samples after arm(), and
+    reports throttle reasons other than gpu_idle. NVML is a fake here: nothing is queried."""
+    import threading
+    import time
+    import types
+
+    calls = []
+    armed_at = []
+    fake = types.SimpleNamespace(
+        NVML_CLOCK_SM=0,
+        nvmlInit=lambda: None,
+        nvmlDeviceGetHandleByIndex=lambda i: i,
+        nvmlDeviceGetMaxClockInfo=lambda h, c: 1965,
+        nvmlDeviceGetClockInfo=lambda h, c: calls.append(time.monotonic()) or 1900,
+        nvmlDeviceGetCurrentClocksEventReasons=lambda h: 0x1 | 0x4,
+    )
+    monkeypatch.setitem(sys.modules, "pynvml", fake)
+    with bench.ClockSampler(0, deferred=True) as clk:
+        warm = len(calls)  # the constructor's warm-up query, discarded
+        time.sleep(0.05)
+        assert len(calls) == warm, "sampled before arm()"
+        armed_at.append(time.monotonic())
+        clk.arm()
+        time.sleep(0.05)
+    s = clk.summary()
+    assert clk.samples and all(t >= armed_at[0] for t in calls[warm:])
+    assert s["samples"] >= 2 and s["sm_mhz"] == 1900 and s["sm_max_mhz"] == 1965
+    assert s["reasons"] == ["sw_power_cap"]
+    assert not any(t.name == clk._t.name and t.is_alive() for t in threading.enumerate())

@@ -78,6 +78,22 @@ typedef struct {
    * determinism suite requires (check_ssa_triton_parity.py:507-562). The generic kernels are
    * deterministic in both modes. Costs extra workspace and some speed. */
   int32_t deterministic;
+  /* Output dropout, fused. The reference applies nn.Dropout(p) to the attention output after its
+   * kernel, in training only (ssa_triton_attention.py:110-113,186-193). dropout_p in [0, 1);
+   * 0 = off (dropout_seed is then not read). When > 0:
+   *   - the forward writes out = O * keep / (1 - p), keep drawn per element from Philox4x32-10
+   *     keyed by dropout_seed (device, two 64-bit values: [0] the key, [1] the counter offset;
+   *     the element with logical index e, its position in contiguous [B, Hq, N, D] or packed
+   *     [T, Hq, D], uses word e % 4 of the call with counter (e / 4, offset));
+   *   - the backward takes that dropped `out` and the gradient of the dropped output as `dout`,
+   *     with the same dropout_p and dropout_seed, and returns the gradients for
+   *     dO = dout * keep / (1 - p): rowsum(out * dout) equals the undropped rowsum(O * dO); the
+   *     kernels read dout * keep (written into the workspace: exact, no rounding of the scaled
+   *     value) and apply 1 / (1 - p) in fp32 through delta and the normaliser.
+   * lse is the undropped normaliser. ssa_attn_bwd_noalloc rejects dropout (no workspace for the
+   * masked dout). */
+  float dropout_p;
+  const uint64_t* dropout_seed;
 } ssa_problem_t;
 
 /* Forward. Replaces ssa_flash_attn_forward (ssa_triton_kernel.py:732-792) and the

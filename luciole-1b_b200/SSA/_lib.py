@@ -49,7 +49,8 @@ class SsaProblem(ctypes.Structure):
                 ("ssa_n", ctypes.c_void_p), ("n_per_head", ctypes.c_int32),
                 ("ssa_b", ctypes.c_void_p), ("cu_seqlens", ctypes.c_void_p),
                 ("max_seqlen", ctypes.c_int32), ("cu_seqlens_padded", ctypes.c_void_p),
-                ("deterministic", ctypes.c_int32)]
+                ("deterministic", ctypes.c_int32), ("dropout_p", ctypes.c_float),
+                ("dropout_seed", ctypes.c_void_p)]
 
 
 def deterministic_default() -> bool:
@@ -172,11 +173,11 @@ def kernel_family_of(prob: "SsaProblem") -> int:
 
 def bwd_workspace_size(prob: "SsaProblem") -> int:
     """ssa_attn_bwd_workspace_size, asked once per problem shape (the size depends on the shape,
-    dtype, causality, head dim, per-head n, packing, the deterministic flag and the q-head-slice
-    override SSA_BWD_HSPLIT, not on pointers)."""
+    dtype, causality, head dim, per-head n, packing, the deterministic flag, whether output dropout
+    is on and the q-head-slice override SSA_BWD_HSPLIT, not on pointers)."""
     key = (prob.dtype, prob.B, prob.Hq, prob.Hkv, prob.N, prob.D, prob.causal,
            prob.softmax_scale > 0, prob.n_per_head, bool(prob.cu_seqlens), prob.max_seqlen,
-           prob.deterministic, os.environ.get("SSA_BWD_HSPLIT"))
+           prob.deterministic, prob.dropout_p > 0, os.environ.get("SSA_BWD_HSPLIT"))
     ws = _ws_cache.get(key)
     if ws is None:
         ws = int(load().ssa_attn_bwd_workspace_size(ctypes.byref(prob)))

@@ -14,6 +14,14 @@ usable and testable without Megatron.
 Additions: ``ssa_n`` may be a per-head list/tensor (``[Hq]``, as the legacy FlexAttention
 variant had); ``packed_seq_params`` (THD + ``cu_seqlens_q``) runs the varlen kernels instead of
 asserting (reference :154-156).
+
+Output dropout (training with ``attention_dropout > 0``). The reference runs ``nn.Dropout`` on the
+kernel's output, inside Megatron's CUDA RNG tracker fork unless sequence parallelism is on
+(reference :186-193). Here the kernels apply it (forward epilogue; the backward's delta pass masks
+the incoming gradient), keyed by a seed drawn from torch's CUDA generator in the same tracker
+context; the distribution is the same, the random stream is the kernels' own. Setting
+``SSA_FUSED_DROPOUT=0`` in the environment restores the reference's ``nn.Dropout`` after the
+kernel.
 """
 
 from __future__ import annotations
@@ -21,6 +29,7 @@ from __future__ import annotations
 import contextlib
 import enum
 import math
+import os
 import warnings
 from typing import Optional
 
@@ -29,6 +38,7 @@ import torch.nn as nn
 from torch import Tensor
 
 from .ssa_flash_attention import ssa_flash_attention, ssa_flash_attn_varlen_func
+from .ssa_triton_kernel import make_dropout_seed
 
 try:  # pragma: no cover - exercised only where megatron-core is installed
     from megatron.core import parallel_state, tensor_parallel
@@ -163,6 +173,26 @@ class SSATritonAttention(MegatronModule):
                 "not to attention probs. Set attention_dropout=0.0 for exact parity.",
                 stacklevel=2)
 
+    def _dropout_seed(self, device) -> Optional[Tensor]:
+        """Seed of the fused output dropout for this call, or None when no dropout runs in the
+        kernels (eval mode, p = 0, or SSA_FUSED_DROPOUT=0). Drawn in the RNG context the
+        reference's nn.Dropout runs in (:186-193)."""
+        if not (self.training and self.dropout_p > 0):
+            return None
+        if os.environ.get("SSA_FUSED_DROPOUT", "1") in ("0", "false", "False"):
+            return None
+        if not getattr(self.config, "sequence_parallel", False):
+            with tensor_parallel.get_cuda_rng_tracker().fork():
+                return make_dropout_seed(device)
+        return make_dropout_seed(device)
+
+    def _eager_dropout(self, context: Tensor) -> Tensor:
+        """The reference's dropout after the kernel (:186-193)."""
+        if not getattr(self.config, "sequence_parallel", False):
+            with tensor_parallel.get_cuda_rng_tracker().fork():
+                return self.attention_dropout(context)
+        return self.attention_dropout(context)
+
     def get_ssa_params(self):
         """Current (n, b) (reference :123-130)."""
         if self.learnable_ssa:
@@ -195,15 +225,13 @@ class SSATritonAttention(MegatronModule):
         if self.force_contiguous_qkv:
             query_t, key_t, value_t = query_t.contiguous(), key_t.contiguous(), value_t.contiguous()
 
+        seed = self._dropout_seed(query.device)
         context = ssa_flash_attention(query_t, key_t, value_t, softmax_scale=self.softmax_scale,
                                       ssa_n=ssa_n, ssa_b=ssa_b, causal=is_causal,
-                                      dropout_p=self.dropout_p, training=self.training)
-        if self.training and self.dropout_p > 0:
-            if not getattr(self.config, "sequence_parallel", False):
-                with tensor_parallel.get_cuda_rng_tracker().fork():
-                    context = self.attention_dropout(context)
-            else:
-                context = self.attention_dropout(context)
+                                      dropout_p=self.dropout_p, training=self.training,
+                                      dropout_seed=seed)
+        if self.training and self.dropout_p > 0 and seed is None:
+            context = self._eager_dropout(context)
         context = _kernel_to_megatron_view(context)
         return context.reshape(*context.size()[:-2], self.hidden_size_per_partition)
 
@@ -234,9 +262,11 @@ class SSATritonAttention(MegatronModule):
         q3 = query.squeeze(1) if squeeze else query
         k3 = key.squeeze(1) if squeeze else key
         v3 = value.squeeze(1) if squeeze else value
+        seed = self._dropout_seed(q3.device)
         out = ssa_flash_attn_varlen_func(q3, k3, v3, cu, int(max_s), self.softmax_scale, ssa_n,
-                                         ssa_b, is_causal, cu_pad)
-        if self.training and self.dropout_p > 0:
-            out = self.attention_dropout(out)
+                                         ssa_b, is_causal, cu_pad, self.dropout_p if seed is not
+                                         None else 0.0, seed)
+        if self.training and self.dropout_p > 0 and seed is None:
+            out = self._eager_dropout(out)
         out = out.reshape(out.shape[0], self.hidden_size_per_partition)
         return out.unsqueeze(1) if squeeze else out

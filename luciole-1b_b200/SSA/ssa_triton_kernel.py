@@ -14,6 +14,9 @@ Differences from the reference, all supersets:
   * packed documents: ``ssa_flash_attn_varlen_forward/backward`` (reference asserts packed
     sequences off, ssa_triton_attention.py:154-156).
   * ``m`` is the same base-2 normaliser M = log2(sum_j exp2(t_j log2 e)) (:248-255).
+  * output dropout fused into the kernels (``dropout_p`` / ``dropout_seed``): the reference applies
+    ``nn.Dropout`` to the kernel's output in its module (ssa_triton_attention.py:186-193); here the
+    forward's epilogue drops and rescales, and the backward's delta pass masks dout.
 """
 
 from __future__ import annotations
@@ -29,7 +32,7 @@ from . import _lib
 __all__ = [
     "ssa_flash_attn_forward", "ssa_flash_attn_backward", "ssa_flash_attn_varlen_forward",
     "ssa_flash_attn_varlen_backward", "warmup_ssa_triton_kernels", "kernel_family",
-    "check_device_status",
+    "check_device_status", "make_dropout_seed",
 ]
 
 
@@ -58,7 +61,8 @@ def _problem(q: torch.Tensor, hkv: int, softmax_scale: float, n: torch.Tensor, b
              per_head: int, causal: bool, B: int, N: int,
              cu_seqlens: Optional[torch.Tensor] = None, max_seqlen: int = 0,
              cu_seqlens_padded: Optional[torch.Tensor] = None,
-             deterministic: bool = False) -> _lib.SsaProblem:
+             deterministic: bool = False, dropout_p: float = 0.0,
+             dropout_seed: Optional[torch.Tensor] = None) -> _lib.SsaProblem:
     if q.dtype not in _lib.DTYPE_CODES:
         raise ValueError(f"unsupported dtype {q.dtype}")
     hq, d = q.shape[1], q.shape[-1]
@@ -67,7 +71,32 @@ def _problem(q: torch.Tensor, hkv: int, softmax_scale: float, n: torch.Tensor, b
         n.data_ptr(), per_head, b.data_ptr(),
         cu_seqlens.data_ptr() if cu_seqlens is not None else None, int(max_seqlen),
         cu_seqlens_padded.data_ptr() if cu_seqlens_padded is not None else None,
-        1 if deterministic else 0)
+        1 if deterministic else 0, float(dropout_p),
+        dropout_seed.data_ptr() if dropout_seed is not None else None)
+
+
+def make_dropout_seed(device) -> torch.Tensor:
+    """A fresh dropout seed: two random 64-bit values (the Philox key and counter offset) drawn on
+    the device from torch's CUDA generator, so the draw needs no host synchronisation, is
+    replayed with fresh values under CUDA-graph capture, and follows torch.manual_seed and
+    Megatron's CUDA RNG tracker (draw it inside the tracker's fork)."""
+    return torch.randint(-(2 ** 63), 2 ** 63 - 1, (2,), dtype=torch.int64,
+                         device=torch.device(device))
+
+
+def _dropout_args(dropout_p, dropout_seed, device):
+    """Validated (p, seed) for the problem block: p = 0 turns dropout off."""
+    p = float(dropout_p or 0.0)
+    if p == 0.0:
+        return 0.0, None
+    if not 0.0 < p < 1.0:
+        raise ValueError(f"dropout_p must be in [0, 1), got {p}")
+    if (dropout_seed is None or not isinstance(dropout_seed, torch.Tensor)
+            or dropout_seed.dtype != torch.int64 or dropout_seed.numel() < 2
+            or dropout_seed.device != device or not dropout_seed.is_contiguous()):
+        raise ValueError("dropout_p > 0 needs dropout_seed: a contiguous int64 tensor of 2 values "
+                         "on the inputs' device (make_dropout_seed)")
+    return p, dropout_seed
 
 
 def _tma_ok(t: torch.Tensor) -> bool:
@@ -127,16 +156,23 @@ def kernel_family(q: torch.Tensor, softmax_scale: float = 1.0) -> int:
     return _lib.load().ssa_attn_kernel_family(ctypes.byref(prob))
 
 
-def ssa_flash_attn_forward(q, k, v, softmax_scale, ssa_n, ssa_b, causal=True):
+def ssa_flash_attn_forward(q, k, v, softmax_scale, ssa_n, ssa_b, causal=True, dropout_p=0.0,
+                           dropout_seed=None):
     """Forward (reference ssa_triton_kernel.py:732-792).
 
     q [B, Hq, N, D], k/v [B, Hkv, N, D] (any strides with a unit D stride; other layouts
     are copied). Returns (out [B, Hq, N, D] with q's dtype and layout, m [B, Hq, N] fp32).
+
+    dropout_p > 0 (with dropout_seed from :func:`make_dropout_seed`) returns the output with
+    dropout applied (elements zeroed with probability p, survivors scaled by 1/(1-p)); m is the
+    undropped normaliser. The backward needs the same p and seed.
     """
     lib = _lib.load()
     B, Hq, Hkv, N, D = _check_qkv(q, k, v)
     n, b, per_head = _params(ssa_n, ssa_b, Hq, q.device)
-    prob = _problem(q, Hkv, softmax_scale, n, b, per_head, causal, B, N)
+    dp, seed = _dropout_args(dropout_p, dropout_seed, q.device)
+    prob = _problem(q, Hkv, softmax_scale, n, b, per_head, causal, B, N, dropout_p=dp,
+                    dropout_seed=seed)
     fam = _lib.kernel_family_of(prob)
     q, k, v = _prep(q, fam), _prep(k, fam), _prep(v, fam)
     out = torch.empty_like(q)
@@ -160,7 +196,7 @@ def _param_grad_pair(n, device):
 
 
 def ssa_flash_attn_backward(q, k, v, out, dout, m, softmax_scale, ssa_n, ssa_b, causal=True,
-                            deterministic=None):
+                            deterministic=None, dropout_p=0.0, dropout_seed=None):
     """Backward (reference ssa_triton_kernel.py:795-897).
 
     Returns (dq, dk, dv, dn, db): dq/dk/dv in the inputs' dtype and layout; dn fp32 with
@@ -171,12 +207,17 @@ def ssa_flash_attn_backward(q, k, v, out, dout, m, softmax_scale, ssa_n, ssa_b, 
     bit-identical from run to run (the reference's determinism rule,
     check_ssa_triton_parity.py:507-562); dk, dv, dn and db are bit-reproducible either way.
     None (default) takes SSA_DETERMINISTIC from the environment (off unless set to 1).
+
+    With output dropout (the forward's dropout_p and dropout_seed), ``out`` is the dropped output
+    the forward returned and ``dout`` the gradient of the dropped output.
     """
     lib = _lib.load()
     B, Hq, Hkv, N, D = _check_qkv(q, k, v)
     n, b, per_head = _params(ssa_n, ssa_b, Hq, q.device)
     det = _lib.deterministic_default() if deterministic is None else bool(deterministic)
-    prob = _problem(q, Hkv, softmax_scale, n, b, per_head, causal, B, N, deterministic=det)
+    dp, seed = _dropout_args(dropout_p, dropout_seed, q.device)
+    prob = _problem(q, Hkv, softmax_scale, n, b, per_head, causal, B, N, deterministic=det,
+                    dropout_p=dp, dropout_seed=seed)
     fam = _lib.kernel_family_of(prob)
     q, k, v, dout = _prep(q, fam), _prep(k, fam), _prep(v, fam), _prep(dout, fam)
     out = _prep(out, fam)
@@ -222,21 +263,24 @@ def _check_padded(cu_seqlens, cu_seqlens_padded):
 
 
 def ssa_flash_attn_varlen_forward(q, k, v, cu_seqlens, max_seqlen, softmax_scale, ssa_n, ssa_b,
-                                  causal=True, cu_seqlens_padded=None):
+                                  causal=True, cu_seqlens_padded=None, dropout_p=0.0,
+                                  dropout_seed=None):
     """Packed documents: q [T, Hq, D], k/v [T, Hkv, D], cu_seqlens int32 [ndoc+1].
 
     Each document attends only within itself (causal or not). Returns (out [T, Hq, D],
     lse [Hq, T] fp32). With cu_seqlens_padded (Megatron's cu_seqlens_q_padded), document z
     starts at row cu_seqlens_padded[z] and the padding rows between documents are ignored; their
     output rows are zero. No reference counterpart: the reference asserts packed sequences off
-    (ssa_triton_attention.py:154-156).
+    (ssa_triton_attention.py:154-156). dropout_p / dropout_seed as in
+    :func:`ssa_flash_attn_forward`.
     """
     lib = _lib.load()
     T, Hq, Hkv, D, ndoc = _check_thd(q, k, v, cu_seqlens)
     cu_pad = _check_padded(cu_seqlens, cu_seqlens_padded)
     n, b, per_head = _params(ssa_n, ssa_b, Hq, q.device)
+    dp, seed = _dropout_args(dropout_p, dropout_seed, q.device)
     prob = _problem(q, Hkv, softmax_scale, n, b, per_head, causal, ndoc, T,
-                    cu_seqlens, max_seqlen, cu_pad)
+                    cu_seqlens, max_seqlen, cu_pad, dropout_p=dp, dropout_seed=seed)
     fam = _lib.kernel_family_of(prob)
     q, k, v = _prep(q, fam), _prep(k, fam), _prep(v, fam)
     alloc = torch.zeros if cu_pad is not None else torch.empty
@@ -252,17 +296,20 @@ def ssa_flash_attn_varlen_forward(q, k, v, cu_seqlens, max_seqlen, softmax_scale
 
 def ssa_flash_attn_varlen_backward(q, k, v, out, dout, lse, cu_seqlens, max_seqlen,
                                    softmax_scale, ssa_n, ssa_b, causal=True,
-                                   cu_seqlens_padded=None, deterministic=None):
+                                   cu_seqlens_padded=None, deterministic=None, dropout_p=0.0,
+                                   dropout_seed=None):
     """Backward of :func:`ssa_flash_attn_varlen_forward`. Returns (dq, dk, dv, dn, db); with
-    cu_seqlens_padded the gradient rows of padding tokens are zero. ``deterministic`` as in
-    :func:`ssa_flash_attn_backward`."""
+    cu_seqlens_padded the gradient rows of padding tokens are zero. ``deterministic`` and the
+    dropout arguments as in :func:`ssa_flash_attn_backward`."""
     lib = _lib.load()
     T, Hq, Hkv, D, ndoc = _check_thd(q, k, v, cu_seqlens)
     cu_pad = _check_padded(cu_seqlens, cu_seqlens_padded)
     n, b, per_head = _params(ssa_n, ssa_b, Hq, q.device)
     det = _lib.deterministic_default() if deterministic is None else bool(deterministic)
+    dp, seed = _dropout_args(dropout_p, dropout_seed, q.device)
     prob = _problem(q, Hkv, softmax_scale, n, b, per_head, causal, ndoc, T,
-                    cu_seqlens, max_seqlen, cu_pad, deterministic=det)
+                    cu_seqlens, max_seqlen, cu_pad, deterministic=det, dropout_p=dp,
+                    dropout_seed=seed)
     fam = _lib.kernel_family_of(prob)
     q, k, v, dout = _prep(q, fam), _prep(k, fam), _prep(v, fam), _prep(dout, fam)
     out = _prep(out, fam)

@@ -5,6 +5,7 @@
 // and carves the caller's workspace, launches on the caller's stream and reports errors as
 // status codes plus a thread-local message. It never allocates device memory.
 #include <atomic>
+#include <cmath>
 #include <cstdarg>
 #include <cstdio>
 #include <cstring>
@@ -57,6 +58,10 @@ int check_problem(const ssa_problem_t* pr) {
     return fail(SSA_ERR_BAD_SHAPE, "varlen needs max_seqlen > 0");
   if (!(pr->softmax_scale == pr->softmax_scale))
     return fail(SSA_ERR_BAD_SHAPE, "softmax_scale is NaN");
+  if (!(pr->dropout_p >= 0.f && pr->dropout_p < 1.f))
+    return fail(SSA_ERR_UNSUPPORTED, "dropout_p must be in [0, 1), got %g", (double)pr->dropout_p);
+  if (pr->dropout_p > 0.f && !pr->dropout_seed)
+    return fail(SSA_ERR_NULL, "dropout_p > 0 needs a dropout_seed device pointer");
   return SSA_OK;
 }
 
@@ -84,6 +89,19 @@ Problem to_problem(const ssa_problem_t* pr) {
   p.cu_seqlens_padded = pr->cu_seqlens ? pr->cu_seqlens_padded : nullptr;
   p.max_seqlen = pr->cu_seqlens ? pr->max_seqlen : pr->N;
   p.det = pr->deterministic ? 1 : 0;
+  if (pr->dropout_p > 0.f) {  // p * 2^24 is exact in double: the threshold is exact too
+    p.drop_thr = (uint32_t)ceil((double)pr->dropout_p * 16777216.0);
+    p.drop_scale = 1.0f / (1.0f - pr->dropout_p);
+    p.drop_delta_scale = 1.0f - pr->dropout_p;
+    p.drop_lse_shift = (float)(-log2(1.0 - (double)pr->dropout_p));
+    p.drop_seed = reinterpret_cast<const unsigned long long*>(pr->dropout_seed);
+  } else {
+    p.drop_thr = 0;
+    p.drop_scale = 1.0f;
+    p.drop_delta_scale = 1.0f;
+    p.drop_lse_shift = 0.0f;
+    p.drop_seed = nullptr;
+  }
   return p;
 }
 
@@ -121,8 +139,11 @@ struct BwdWorkspace {
   float* db_part;
   void* sm100;
   size_t sm100_bytes;
+  void* dom;  // output dropout: dout * keep / (1 - p) in the logical contiguous layout
   size_t total;
 };
+
+size_t dtype_bytes(int dtype) { return dtype == SSA_DTYPE_F32 ? 4 : 2; }
 
 BwdWorkspace carve_bwd(const ssa_problem_t* pr, void* base) {
   const Problem p = to_problem(pr);
@@ -143,6 +164,11 @@ BwdWorkspace carve_bwd(const ssa_problem_t* pr, void* base) {
     off += part;
     w.db_part = reinterpret_cast<float*>(b ? b + off : nullptr);
     off += part;
+  }
+  w.dom = nullptr;
+  if (pr->dropout_p > 0.f) {  // dout * keep, then the shifted lse (dropout_scratch_bytes)
+    w.dom = b ? b + off : nullptr;
+    off += dropout_scratch_bytes(p, (int)dtype_bytes(pr->dtype));
   }
   w.total = off;
   return w;
@@ -296,6 +322,7 @@ int ssa_attn_bwd_preprocess(const ssa_problem_t* prob, ssa_tensor_t out, ssa_ten
   if ((rc = bind_device(out.ptr, "out")) != SSA_OK) return rc;
   const Problem p = to_problem(prob);
   return finish_launch(launch_bwd_preprocess(prob->dtype, p, to_ref(out), to_ref(dout), delta,
+                                             nullptr, nullptr, nullptr,
                                              static_cast<cudaStream_t>(stream)),
                        "ssa_attn_bwd_preprocess");
 }
@@ -338,14 +365,19 @@ int ssa_attn_bwd(const ssa_problem_t* prob, ssa_tensor_t q, ssa_tensor_t k, ssa_
       return fail(SSA_ERR_BAD_STRIDE, "out: base and strides must be 16-byte aligned");
     return finish_launch(launch_bwd_sm100(prob->dtype, p, to_ref(q), to_ref(k), to_ref(v),
                                           to_ref(out), to_ref(dout), lse, w.delta, to_ref(dq),
-                                          to_ref(dk), to_ref(dv), dn, db, w.sm100, w.sm100_bytes,
-                                          st),
+                                          to_ref(dk), to_ref(dv), dn, db, w.dom, w.sm100,
+                                          w.sm100_bytes, st),
                          "ssa_attn_bwd(sm100)");
   }
-  rc = launch_bwd_preprocess(prob->dtype, p, to_ref(out), to_ref(dout), w.delta, st);
+  float* lse_sh = w.dom ? dropout_lse_buffer(p, w.dom, (int)dtype_bytes(prob->dtype)) : nullptr;
+  rc = launch_bwd_preprocess(prob->dtype, p, to_ref(out), to_ref(dout), w.delta, w.dom, lse,
+                             lse_sh, st);
   if ((rc = finish_launch(rc, "ssa_attn_bwd(preprocess)")) != SSA_OK) return rc;
-  rc = launch_bwd_generic(prob->dtype, p, to_ref(q), to_ref(k), to_ref(v), to_ref(dout), lse,
-                          w.delta, to_ref(dq), to_ref(dk), to_ref(dv), w.dn_part, w.db_part, st);
+  // with output dropout the gradient kernels read dout * keep and the shifted lse
+  const TensorRef dO = w.dom ? dropout_dout_ref(p, w.dom) : to_ref(dout);
+  rc = launch_bwd_generic(prob->dtype, p, to_ref(q), to_ref(k), to_ref(v), dO,
+                          lse_sh ? lse_sh : lse, w.delta, to_ref(dq), to_ref(dk), to_ref(dv),
+                          w.dn_part, w.db_part, st);
   if ((rc = finish_launch(rc, "ssa_attn_bwd(generic)")) != SSA_OK) return rc;
   rc = launch_dndb_reduce(w.dn_part, w.db_part, p.B, p.Hq, generic_bwd_partials_per_seq(p),
                           p.n_per_head, dn, db, st);

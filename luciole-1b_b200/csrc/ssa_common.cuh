@@ -37,6 +37,18 @@ struct Problem {
   const int* cu_seqlens_padded;  // packed with padding: start row of each document, or nullptr
   int max_seqlen;                // rows a sequence can have (N when dense)
   int det;                       // tensor-core backward: bit-reproducible dq (ordered dQ adds)
+  // Output dropout (0 = off): keep an element iff its Philox word >> 8 >= drop_thr
+  // (= ceil(p * 2^24)); the forward scales kept elements by drop_scale (= 1 / (1 - p), fp32).
+  // The backward runs on dout * keep (exact in any dtype) and moves the 1 / (1 - p) into fp32
+  // quantities instead: delta is multiplied by drop_delta_scale (= 1 - p) and every lse read
+  // by the backward kernels is lowered by drop_lse_shift (= log2(1 / (1 - p))), so P comes out
+  // multiplied by 1 / (1 - p). Then P (dP - delta) and P^T dO are the gradients of the scaled
+  // dO without a rounding of dout / (1 - p) to 16 bits. Off: 1, 1, 0.
+  uint32_t drop_thr;
+  float drop_scale;
+  float drop_delta_scale;
+  float drop_lse_shift;
+  const unsigned long long* drop_seed;  // device: [0] Philox key, [1] counter offset
 };
 
 struct TensorRef {
@@ -68,6 +80,53 @@ __device__ __forceinline__ int64_t stat_offset(const Problem& p, int z, int h, i
                                                int row) {
   if (p.cu_seqlens) return (int64_t)h * p.N + seq_start + row;  // N == T (total tokens)
   return ((int64_t)z * p.Hq + h) * p.N + row;
+}
+
+// ---------------------------------------------------------------------------------------------
+// Output dropout. The reference drops attention-output elements with nn.Dropout after its kernel
+// (training/train/train_ssa_triton/SSA/ssa_triton_attention.py:110-113,186-193); here the forward
+// epilogue applies the mask and the backward's delta pass applies it to dout. Keep decisions come
+// from Philox4x32-10 (Salmon, Moraes, Dror, Shaw, "Parallel random numbers: as easy as 1, 2, 3",
+// SC 2011): ten rounds of two 32x32->64-bit products with the paper's multipliers, the key
+// advanced by the paper's Weyl increments between rounds. Element e (its position in the
+// logical contiguous output: ((z * Hq + h) * N + row) * D + d dense, (t * Hq + h) * D + d
+// packed) takes word e % 4 of the call with counter (e / 4, offset) and key seed.
+
+__device__ __forceinline__ uint4 philox4x32_10(uint4 c, uint32_t k0, uint32_t k1) {
+#pragma unroll
+  for (int r = 0; r < 10; ++r) {
+    const uint32_t lo0 = 0xD2511F53u * c.x, hi0 = __umulhi(0xD2511F53u, c.x);
+    const uint32_t lo1 = 0xCD9E8D57u * c.z, hi1 = __umulhi(0xCD9E8D57u, c.z);
+    c = make_uint4(hi1 ^ c.y ^ k0, lo1, hi0 ^ c.w ^ k1, lo0);
+    k0 += 0x9E3779B9u;
+    k1 += 0xBB67AE85u;
+  }
+  return c;
+}
+
+// Index of element (z, h, row, d = 0), row relative to seq_start.
+__device__ __forceinline__ uint64_t dropout_index(const Problem& p, int z, int h, int seq_start,
+                                                  int row) {
+  if (p.cu_seqlens) return ((uint64_t)(seq_start + row) * p.Hq + h) * (uint64_t)p.D;
+  return (((uint64_t)z * p.Hq + h) * p.N + row) * (uint64_t)p.D;
+}
+
+struct DropoutKey {
+  uint32_t k0, k1, o0, o1, thr;
+};
+__device__ __forceinline__ DropoutKey dropout_key(const Problem& p) {
+  const unsigned long long key = __ldg(p.drop_seed), off = __ldg(p.drop_seed + 1);
+  return DropoutKey{(uint32_t)key, (uint32_t)(key >> 32), (uint32_t)off, (uint32_t)(off >> 32),
+                    p.drop_thr};
+}
+
+// Keep bits of the four elements e .. e + 3 (e a multiple of 4): bit i for element e + i.
+__device__ __forceinline__ uint32_t dropout_keep4(const DropoutKey& k, uint64_t e) {
+  const uint64_t c = e >> 2;
+  const uint4 w = philox4x32_10(make_uint4((uint32_t)c, (uint32_t)(c >> 32), k.o0, k.o1), k.k0,
+                                k.k1);
+  return (uint32_t)((w.x >> 8) >= k.thr) | ((uint32_t)((w.y >> 8) >= k.thr) << 1) |
+         ((uint32_t)((w.z >> 8) >= k.thr) << 2) | ((uint32_t)((w.w >> 8) >= k.thr) << 3);
 }
 
 __device__ __forceinline__ float load_n(const Problem& p, int hq) {

@@ -137,17 +137,35 @@ __global__ void __launch_bounds__(kNT) fwd_generic_kernel(Problem p, TensorRef q
     const float l_safe = l_run > 0.f ? l_run : 1.f;
     const float inv_l = 1.f / l_safe;
     T* ob = reinterpret_cast<T*>(o.ptr) + row_offset(o, p, z, hq, seq_start, row);
+    if (p.drop_seed) {  // output dropout: column sub + 4e is word `sub` of group e's Philox call
+      const DropoutKey dk = dropout_key(p);
+      const uint64_t e0 = dropout_index(p, z, hq, seq_start, row);
+      const float ks = inv_l * p.drop_scale;
+#pragma unroll 4
+      for (int e = 0; e < DPT; ++e) {
+        const bool keep = (dropout_keep4(dk, e0 + 4 * e) >> sub) & 1u;
+        ob[sub + 4 * e] = from_f32<T>(keep ? acc[e] * ks : 0.f);
+      }
+    } else {
 #pragma unroll
-    for (int e = 0; e < DPT; ++e) ob[sub + 4 * e] = from_f32<T>(acc[e] * inv_l);
+      for (int e = 0; e < DPT; ++e) ob[sub + 4 * e] = from_f32<T>(acc[e] * inv_l);
+    }
     if (sub == 0) lse[stat_offset(p, z, hq, seq_start, row)] = m_run + log2f(l_safe);
   }
 }
 
 // ---------------------------------------------------------------------------------------------
 // delta = rowsum(O * dO) in fp32 (ssa_triton_kernel.py:267-298).
+// With output dropout (p.drop_seed set) `o` is the dropped output and `dout` the gradient of the
+// dropped output: rowsum(o * dout) is the undropped rowsum(O * dO) with dO = dout * keep / (1 - p).
+// dout * keep goes to `dom` (contiguous in the logical layout), delta is stored times (1 - p) and
+// lse lowered by log2(1 / (1 - p)) goes to `lse_shifted`; with these the gradient kernels produce
+// the gradients of dO.
 template <typename T>
 __global__ void __launch_bounds__(kNT) bwd_preprocess_kernel(Problem p, TensorRef o,
-                                                             TensorRef dout, float* delta) {
+                                                             TensorRef dout, float* delta, T* dom,
+                                                             const float* lse,
+                                                             float* lse_shifted) {
   const int r = threadIdx.x >> 2, sub = threadIdx.x & 3;
   const int z = blockIdx.y / p.Hq, hq = blockIdx.y % p.Hq;
   int seq_start, L;
@@ -159,9 +177,22 @@ __global__ void __launch_bounds__(kNT) bwd_preprocess_kernel(Problem p, TensorRe
     const T* ob = reinterpret_cast<const T*>(o.ptr) + row_offset(o, p, z, hq, seq_start, row);
     const T* db = reinterpret_cast<const T*>(dout.ptr) + row_offset(dout, p, z, hq, seq_start, row);
     for (int d = sub; d < p.D; d += 4) acc = fmaf(to_f32<T>(ob[d]), to_f32<T>(db[d]), acc);
+    if (dom) {
+      const DropoutKey dk = dropout_key(p);
+      const uint64_t e0 = dropout_index(p, z, hq, seq_start, row);
+      for (int d = sub; d < p.D; d += 4) {
+        const bool keep = (dropout_keep4(dk, e0 + (d - sub)) >> sub) & 1u;
+        dom[e0 + d] = keep ? db[d] : from_f32<T>(0.f);
+      }
+      acc *= p.drop_delta_scale;
+    }
   }
   acc = quad_sum(acc);
-  if (row < L && sub == 0) delta[stat_offset(p, z, hq, seq_start, row)] = acc;
+  if (row < L && sub == 0) {
+    const int64_t so = stat_offset(p, z, hq, seq_start, row);
+    delta[so] = acc;
+    if (dom) lse_shifted[so] = lse[so] - p.drop_lse_shift;
+  }
 }
 
 // ---------------------------------------------------------------------------------------------
@@ -436,12 +467,12 @@ int launch_fwd_generic(int dtype, const Problem& p, TensorRef q, TensorRef k, Te
 }
 
 int launch_bwd_preprocess(int dtype, const Problem& p, TensorRef o, TensorRef dout, float* delta,
-                          cudaStream_t st) {
+                          void* dom, const float* lse, float* lse_shifted, cudaStream_t st) {
   dim3 grid((p.max_seqlen + kBM - 1) / kBM, p.B * p.Hq);
   switch (dtype) {
-    case SSA_DTYPE_F32: bwd_preprocess_kernel<float><<<grid, kNT, 0, st>>>(p, o, dout, delta); break;
-    case SSA_DTYPE_F16: bwd_preprocess_kernel<__half><<<grid, kNT, 0, st>>>(p, o, dout, delta); break;
-    case SSA_DTYPE_BF16: bwd_preprocess_kernel<__nv_bfloat16><<<grid, kNT, 0, st>>>(p, o, dout, delta); break;
+    case SSA_DTYPE_F32: bwd_preprocess_kernel<float><<<grid, kNT, 0, st>>>(p, o, dout, delta, static_cast<float*>(dom), lse, lse_shifted); break;
+    case SSA_DTYPE_F16: bwd_preprocess_kernel<__half><<<grid, kNT, 0, st>>>(p, o, dout, delta, static_cast<__half*>(dom), lse, lse_shifted); break;
+    case SSA_DTYPE_BF16: bwd_preprocess_kernel<__nv_bfloat16><<<grid, kNT, 0, st>>>(p, o, dout, delta, static_cast<__nv_bfloat16*>(dom), lse, lse_shifted); break;
     default: return SSA_ERR_UNSUPPORTED;
   }
   note_launches(1);

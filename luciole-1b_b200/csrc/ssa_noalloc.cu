@@ -73,6 +73,10 @@ extern "C" int ssa_attn_bwd_noalloc(const ssa_problem_t* pr, ssa_tensor_t q, ssa
       (rc = abi_check_tensor(dk, "dk")) || (rc = abi_check_tensor(dv, "dv")))
     return rc;
   if (!lse || !dn || !db) return abi_error(SSA_ERR_NULL, "lse / dn / db is NULL");
+  if (pr->dropout_p > 0.f)
+    return abi_error(SSA_ERR_UNSUPPORTED,
+                     "ssa_attn_bwd_noalloc: output dropout needs a workspace for the masked dout; "
+                     "use ssa_attn_bwd");
   const Problem p = abi_to_problem(pr);
 
   // Scratch layout: delta [Hq x rows] fp32, then dn and db partials [B x Hq x tiles] fp32.
@@ -101,7 +105,7 @@ extern "C" int ssa_attn_bwd_noalloc(const ssa_problem_t* pr, ssa_tensor_t q, ssa
       tv{v.ptr, v.sB, v.sH, v.sN}, to{out.ptr, out.sB, out.sH, out.sN},
       tdo{dout.ptr, dout.sB, dout.sH, dout.sN}, tdq{dq.ptr, dq.sB, dq.sH, dq.sN},
       tdk{dk.ptr, dk.sB, dk.sH, dk.sN}, tdv{dv.ptr, dv.sB, dv.sH, dv.sN};
-  rc = launch_bwd_preprocess(pr->dtype, p, to, tdo, delta, st);
+  rc = launch_bwd_preprocess(pr->dtype, p, to, tdo, delta, nullptr, nullptr, nullptr, st);
   if (rc == SSA_OK)
     rc = launch_bwd_generic(pr->dtype, p, tq, tk, tv, tdo, lse, delta, tdq, tdk, tdv, dn_part,
                             db_part, st);

@@ -783,7 +783,9 @@ __global__ void __launch_bounds__(256) bwd_preprocess_sm100_kernel(Problem p, Te
                                                                    TensorRef dout, float* delta,
                                                                    float* dq_accum,
                                                                    int64_t dq_rows, int* sem,
-                                                                   int sem_per_zh) {
+                                                                   int sem_per_zh, T* dom,
+                                                                   const float* lse,
+                                                                   float* lse_shifted) {
   griddep_launch_dependents();  // the backward's setup may overlap this pass
   if (sem && blockIdx.x == 0) {
     const int nz = p.cu_seqlens ? p.B : 1;  // packed: grid row = q-head, every document
@@ -828,12 +830,29 @@ __global__ void __launch_bounds__(256) bwd_preprocess_sm100_kernel(Problem p, Te
     const T* be = reinterpret_cast<const T*>(&b);
 #pragma unroll
     for (int i = 0; i < 8; ++i) acc = fmaf(to_f32<T>(ae[i]), to_f32<T>(be[i]), acc);
+    if (dom) {
+      // Output dropout: o is the dropped output and dout the gradient of the dropped output, so
+      // the sum above is the undropped rowsum(O * dO) with dO = dout * keep / (1 - p). The main
+      // kernel reads dout * keep (dom, exact) with delta * (1 - p) and lse lowered by
+      // log2(1 / (1 - p)) (lse_shifted, written below), which gives the gradients of dO.
+      const DropoutKey dk = dropout_key(p);
+      const uint64_t e0 = dropout_index(p, z, hq, 0, row) + (uint64_t)(sub * 8);
+      const uint32_t keep = dropout_keep4(dk, e0) | (dropout_keep4(dk, e0 + 4) << 4);
+      uint4 m = b;
+      uint16_t* me = reinterpret_cast<uint16_t*>(&m);
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        if (!((keep >> i) & 1u)) me[i] = 0;
+      *reinterpret_cast<uint4*>(dom + e0) = m;
+      acc *= p.drop_delta_scale;
+    }
   }
 #pragma unroll
   for (int o2 = 1; o2 < TPR; o2 <<= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o2);
   if (valid && sub == 0) {
     const int64_t so = p.cu_seqlens ? (int64_t)hq * p.N + row : ((int64_t)z * p.Hq + hq) * p.N + row;
     delta[so] = acc;
+    if (dom) lse_shifted[so] = __ldg(lse + so) - p.drop_lse_shift;
   }
 }
 
@@ -1561,23 +1580,31 @@ BwdLayout bwd_layout(const Problem& p) {
 template <bool BF16>
 int run_bwd(const Problem& p, TensorRef q, TensorRef k, TensorRef v, TensorRef out,
             TensorRef dout, const float* lse, float* delta, TensorRef dq, TensorRef dk,
-            TensorRef dv, float* dn, float* db, void* ws, size_t ws_bytes, cudaStream_t st) {
+            TensorRef dv, float* dn, float* db, void* dom, void* ws, size_t ws_bytes,
+            cudaStream_t st) {
   using C = BwdCfg;
+  using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
   const int dtype = BF16 ? SSA_DTYPE_BF16 : SSA_DTYPE_F16;
   const BwdLayout lay = bwd_layout(p);
   if (!ws || ws_bytes < lay.total) return SSA_ERR_WORKSPACE;
+  if (p.drop_seed && !dom) return SSA_ERR_WORKSPACE;
+  T* domT = p.drop_seed ? static_cast<T*>(dom) : nullptr;
+  float* lse_sh = domT ? dropout_lse_buffer(p, dom) : nullptr;
   CUtensorMap tq, tk, tv, tdo;
   int rc;
   if ((rc = make_tmap_bhnd(&tq, q, p, dtype, p.Hq, C::BT)) != SSA_OK) return rc;
   if ((rc = make_tmap_bhnd(&tk, k, p, dtype, p.Hkv, C::BN)) != SSA_OK) return rc;
   if ((rc = make_tmap_bhnd(&tv, v, p, dtype, p.Hkv, C::BN)) != SSA_OK) return rc;
-  if ((rc = make_tmap_bhnd(&tdo, dout, p, dtype, p.Hq, C::BT)) != SSA_OK) return rc;
+  // with output dropout the main kernel reads the masked dout the preprocess writes
+  if ((rc = make_tmap_bhnd(&tdo, domT ? dropout_dout_ref(p, domT) : dout, p, dtype, p.Hq,
+                           C::BT)) != SSA_OK)
+    return rc;
   uint8_t* w = static_cast<uint8_t*>(ws);
   BwdArgs a;
   a.p = p;
   a.dk = dk;
   a.dv = dv;
-  a.lse = lse;
+  a.lse = lse_sh ? lse_sh : lse;
   a.delta = delta;
   a.dq_accum = reinterpret_cast<float*>(w);
   a.dq_rows = lay.dq_rows;
@@ -1594,16 +1621,17 @@ int run_bwd(const Problem& p, TensorRef q, TensorRef k, TensorRef v, TensorRef o
   a.dq_sem = p.det ? reinterpret_cast<int*>(w + lay.dq_bytes + 2 * lay.part_bytes + lay.dkv_bytes)
                    : nullptr;
   {
-    using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
     const unsigned gy = p.cu_seqlens ? p.Hq : p.B * p.Hq;
     if (p.D == 32)
       bwd_preprocess_sm100_kernel<T, 32, 64>
           <<<dim3((unsigned)((lay.dq_rows + 63) / 64), gy), 256, 0, st>>>(
-              p, out, dout, delta, a.dq_accum, lay.dq_rows, a.dq_sem, 4 * lay.ntq);
+              p, out, dout, delta, a.dq_accum, lay.dq_rows, a.dq_sem, 4 * lay.ntq, domT, lse,
+              lse_sh);
     else
       bwd_preprocess_sm100_kernel<T, 64, 64>
           <<<dim3((unsigned)((lay.dq_rows + 31) / 32), gy), 256, 0, st>>>(
-              p, out, dout, delta, a.dq_accum, lay.dq_rows, a.dq_sem, 4 * lay.ntq);
+              p, out, dout, delta, a.dq_accum, lay.dq_rows, a.dq_sem, 4 * lay.ntq, domT, lse,
+              lse_sh);
     note_launches(1);
   }
   // dQ accumulator as a 2-D fp32 tensor [rows][64] for the drain's tiled reduce-adds:
@@ -1630,7 +1658,6 @@ int run_bwd(const Problem& p, TensorRef q, TensorRef k, TensorRef v, TensorRef o
                  tdq, a) != cudaSuccess)
     return SSA_ERR_LAUNCH;
   note_launches(1);
-  using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
   if (p.D == 32)
     return launch_dq_convert_dndb<T, 32, 64>(p, a.dq_accum, a.dq_rows, dq, a.dn_part, a.db_part,
                                              lay.ppk * lay.nkv, dn, db, a, st);
@@ -1641,24 +1668,30 @@ int run_bwd(const Problem& p, TensorRef q, TensorRef k, TensorRef v, TensorRef o
 template <bool BF16>
 int run_bwd128(const Problem& p, TensorRef q, TensorRef k, TensorRef v, TensorRef out,
                TensorRef dout, const float* lse, float* delta, TensorRef dq, TensorRef dk,
-               TensorRef dv, float* dn, float* db, void* ws, size_t ws_bytes, cudaStream_t st) {
+               TensorRef dv, float* dn, float* db, void* dom, void* ws, size_t ws_bytes,
+               cudaStream_t st) {
   using C = Bwd128Cfg;
   using T = typename std::conditional<BF16, __nv_bfloat16, __half>::type;
   const int dtype = BF16 ? SSA_DTYPE_BF16 : SSA_DTYPE_F16;
   const BwdLayout lay = bwd_layout(p);
   if (!ws || ws_bytes < lay.total) return SSA_ERR_WORKSPACE;
+  if (p.drop_seed && !dom) return SSA_ERR_WORKSPACE;
+  T* domT = p.drop_seed ? static_cast<T*>(dom) : nullptr;
+  float* lse_sh = domT ? dropout_lse_buffer(p, dom) : nullptr;
   CUtensorMap tq, tk, tv, tdo, tdq;
   int rc;
   if ((rc = make_tmap_bhnd(&tq, q, p, dtype, p.Hq, C::BT)) != SSA_OK) return rc;
   if ((rc = make_tmap_bhnd(&tk, k, p, dtype, p.Hkv, C::BN)) != SSA_OK) return rc;
   if ((rc = make_tmap_bhnd(&tv, v, p, dtype, p.Hkv, C::BN)) != SSA_OK) return rc;
-  if ((rc = make_tmap_bhnd(&tdo, dout, p, dtype, p.Hq, C::BT)) != SSA_OK) return rc;
+  if ((rc = make_tmap_bhnd(&tdo, domT ? dropout_dout_ref(p, domT) : dout, p, dtype, p.Hq,
+                           C::BT)) != SSA_OK)
+    return rc;
   uint8_t* w = static_cast<uint8_t*>(ws);
   BwdArgs a;
   a.p = p;
   a.dk = dk;
   a.dv = dv;
-  a.lse = lse;
+  a.lse = lse_sh ? lse_sh : lse;
   a.delta = delta;
   a.dq_accum = reinterpret_cast<float*>(w);
   a.dq_rows = lay.dq_rows;
@@ -1676,8 +1709,8 @@ int run_bwd128(const Problem& p, TensorRef q, TensorRef k, TensorRef v, TensorRe
                    : nullptr;
   {
     dim3 gp((unsigned)((lay.dq_rows + 15) / 16), p.cu_seqlens ? p.Hq : p.B * p.Hq);
-    bwd_preprocess_sm100_kernel<T, 128, 128><<<gp, 256, 0, st>>>(p, out, dout, delta, a.dq_accum,
-                                                             lay.dq_rows, a.dq_sem, 4 * lay.ntq);
+    bwd_preprocess_sm100_kernel<T, 128, 128><<<gp, 256, 0, st>>>(
+        p, out, dout, delta, a.dq_accum, lay.dq_rows, a.dq_sem, 4 * lay.ntq, domT, lse, lse_sh);
   }
   {  // dQ accumulator as 2-D fp32 [rows][128]; {32 head dims x 64 queries} boxes, no swizzle
     auto enc = tmap_encoder();
@@ -1712,20 +1745,20 @@ size_t sm100_bwd_workspace_bytes(const Problem& p) { return sm100::bwd_layout(p)
 
 int launch_bwd_sm100(int dtype, const Problem& p, TensorRef q, TensorRef k, TensorRef v,
                      TensorRef out, TensorRef dout, const float* lse, float* delta, TensorRef dq,
-                     TensorRef dk, TensorRef dv, float* dn, float* db, void* ws, size_t ws_bytes,
-                     cudaStream_t st) {
+                     TensorRef dk, TensorRef dv, float* dn, float* db, void* dom, void* ws,
+                     size_t ws_bytes, cudaStream_t st) {
   if (p.D == 128)
     return dtype == SSA_DTYPE_BF16
                ? sm100::run_bwd128<true>(p, q, k, v, out, dout, lse, delta, dq, dk, dv, dn, db,
-                                         ws, ws_bytes, st)
+                                         dom, ws, ws_bytes, st)
                : sm100::run_bwd128<false>(p, q, k, v, out, dout, lse, delta, dq, dk, dv, dn, db,
-                                          ws, ws_bytes, st);
+                                          dom, ws, ws_bytes, st);
   if (p.D != 64 && p.D != 32) return SSA_ERR_UNSUPPORTED;
   return dtype == SSA_DTYPE_BF16
-             ? sm100::run_bwd<true>(p, q, k, v, out, dout, lse, delta, dq, dk, dv, dn, db, ws,
-                                    ws_bytes, st)
-             : sm100::run_bwd<false>(p, q, k, v, out, dout, lse, delta, dq, dk, dv, dn, db, ws,
-                                     ws_bytes, st);
+             ? sm100::run_bwd<true>(p, q, k, v, out, dout, lse, delta, dq, dk, dv, dn, db, dom,
+                                    ws, ws_bytes, st)
+             : sm100::run_bwd<false>(p, q, k, v, out, dout, lse, delta, dq, dk, dv, dn, db, dom,
+                                     ws, ws_bytes, st);
 }
 
 }  // namespace ssa

@@ -412,11 +412,24 @@ __global__ void __launch_bounds__(192, 2)
         // p.D is the tensors' head dim: 32 when a D = 32 problem runs this D = 64 kernel (its
         // TMA boxes zero-fill columns 32..63, so those O columns are zero and not stored).
         if (row < L && c * 32 < p.D) {
+          if (p.drop_seed) {  // output dropout: dropped elements 0, kept ones scaled by 1/(1-p)
+            const DropoutKey dk = dropout_key(p);
+            const uint64_t e0 = dropout_index(p, z, hq, seq_start, row) + (uint64_t)(c * 32);
+            const float ks = inv_l * p.drop_scale;
+            uint32_t keep = 0;
+#pragma unroll
+            for (int g = 0; g < 8; ++g) keep |= dropout_keep4(dk, e0 + 4 * g) << (4 * g);
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              o[i] = __float_as_uint(((keep >> i) & 1u) ? __uint_as_float(o[i]) * ks : 0.f);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * inv_l);
+          }
           uint32_t w[16];
 #pragma unroll
           for (int i = 0; i < 16; ++i)
-            w[i] = pack2<BF16>(__uint_as_float(o[2 * i]) * inv_l,
-                               __uint_as_float(o[2 * i + 1]) * inv_l);
+            w[i] = pack2<BF16>(__uint_as_float(o[2 * i]), __uint_as_float(o[2 * i + 1]));
           uint4* dst = reinterpret_cast<uint4*>(orow + c * 32);
 #pragma unroll
           for (int i = 0; i < 4; ++i)

@@ -119,3 +119,49 @@ def test_make_graphed_callables_module(cuda_device):
     _close("dk", k.grad, ke.grad)
     _close("dv", v.grad, ve.grad)
     _close("dn", n_grad_graph, mod.ssa_n_raw.grad)
+
+
+def test_capture_with_fused_dropout(cuda_device):
+    """Output dropout under capture: the seed is drawn inside the graph from torch's CUDA
+    generator, so every replay draws a fresh mask, and each replay's output is the undropped
+    output masked by the oracle's Philox mask for the seed that replay drew."""
+    from oracle.ssa_dropout import keep_mask_dense, keep_scale, seed_pair
+    from SSA.ssa_flash_attention import ssa_flash_attention
+    from SSA.ssa_triton_kernel import make_dropout_seed
+    dev = cuda_device
+    B, Hq, Hkv, N, D, p = 1, 4, 2, 256, 64, 0.3
+    g = torch.Generator(device="cpu").manual_seed(11)
+    q, k, v = ((torch.randn(B, h, N, D, generator=g) * 0.5).to(torch.bfloat16).to(dev)
+               for h in (Hq, Hkv, Hkv))
+    n, b = torch.tensor(0.5, device=dev), torch.tensor(0.8, device=dev)
+    seed_out = torch.zeros(2, dtype=torch.int64, device=dev)
+
+    def step():
+        seed = make_dropout_seed(dev)
+        seed_out.copy_(seed)
+        return ssa_flash_attention(q, k, v, D ** -0.5, n, b, True, dropout_p=p, training=True,
+                                   dropout_seed=seed)
+
+    side = torch.cuda.Stream(dev)
+    side.wait_stream(torch.cuda.current_stream(dev))
+    with torch.cuda.stream(side):
+        step()
+    torch.cuda.current_stream(dev).wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        out = step()
+    plain = ssa_flash_attention(q, k, v, D ** -0.5, n, b, True).double().cpu()
+    masks = []
+    for _ in range(2):
+        graph.replay()
+        torch.cuda.synchronize()
+        s0, s1 = seed_pair(seed_out)
+        keep = torch.from_numpy(keep_mask_dense(B, Hq, N, D, s0, s1, p))
+        got = out.double().cpu()
+        assert (got[~keep] == 0).all()
+        want = plain * keep_scale(p)
+        kept = keep & (plain != 0)
+        assert ((got - want).abs()[kept] <= 2.0 ** -6 * want.abs()[kept]).all()
+        masks.append(keep)
+    assert not torch.equal(masks[0], masks[1]), "replays must draw fresh masks"
+    del graph

@@ -16,6 +16,8 @@
 #include <cuda.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "ssa_common.cuh"
 
 namespace ssa {
@@ -113,6 +115,25 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
 __device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 __device__ __forceinline__ void griddep_launch_dependents() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Launch with programmatic stream serialization (the kernel may start before the previous one on
+// the stream has finished; it calls griddep_wait() before touching global memory that kernel
+// writes or reads).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                       Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
 // D[tmem] (+)= A[smem desc] * B[smem desc]

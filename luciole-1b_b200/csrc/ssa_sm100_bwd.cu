@@ -787,6 +787,9 @@ __global__ void __launch_bounds__(256) bwd_preprocess_sm100_kernel(Problem p, Te
                                                                    const float* lse,
                                                                    float* lse_shifted) {
   griddep_launch_dependents();  // the backward's setup may overlap this pass
+  // Launched programmatically behind the forward (which wrote `o`): nothing global is touched
+  // before that grid has completed.
+  griddep_wait();
   if (sem && blockIdx.x == 0) {
     const int nz = p.cu_seqlens ? p.B : 1;  // packed: grid row = q-head, every document
     for (int zz = 0; zz < nz; ++zz) {
@@ -881,6 +884,7 @@ __global__ void __launch_bounds__(256) dq_convert_kernel(Problem p, const float*
                                                          int64_t dq_rows, TensorRef dq,
                                                          DndbArgs r) {
   griddep_wait();  // launched programmatically behind the backward kernel
+  griddep_launch_dependents();  // the next forward may launch; it waits for this grid first
   // After a device timeout (this backward's or an earlier launch's) dq, dk, dv, dn and db are NaN.
   if ((int)blockIdx.y < r.rows) {
     const bool failed = block_status_failed(r.status);
@@ -966,24 +970,6 @@ __global__ void __launch_bounds__(256) dq_convert_kernel(Problem p, const float*
                    pack2<false>(a1.z, a1.w));
   }
   *reinterpret_cast<uint4*>(d) = w;
-}
-
-// Launch with programmatic stream serialization (the kernel may start before the previous one on
-// the stream has finished; it calls griddep_wait() before touching that kernel's results).
-template <typename... KArgs, typename... Args>
-cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
-                       Args&&... args) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid;
-  cfg.blockDim = block;
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
 // dq conversion + dn / db reduction, one launch.
@@ -1622,16 +1608,17 @@ int run_bwd(const Problem& p, TensorRef q, TensorRef k, TensorRef v, TensorRef o
                    : nullptr;
   {
     const unsigned gy = p.cu_seqlens ? p.Hq : p.B * p.Hq;
-    if (p.D == 32)
-      bwd_preprocess_sm100_kernel<T, 32, 64>
-          <<<dim3((unsigned)((lay.dq_rows + 63) / 64), gy), 256, 0, st>>>(
-              p, out, dout, delta, a.dq_accum, lay.dq_rows, a.dq_sem, 4 * lay.ntq, domT, lse,
-              lse_sh);
-    else
-      bwd_preprocess_sm100_kernel<T, 64, 64>
-          <<<dim3((unsigned)((lay.dq_rows + 31) / 32), gy), 256, 0, st>>>(
-              p, out, dout, delta, a.dq_accum, lay.dq_rows, a.dq_sem, 4 * lay.ntq, domT, lse,
-              lse_sh);
+    const cudaError_t e =
+        p.D == 32
+            ? launch_pdl(bwd_preprocess_sm100_kernel<T, 32, 64>,
+                         dim3((unsigned)((lay.dq_rows + 63) / 64), gy), dim3(256), 0, st, p, out,
+                         dout, delta, a.dq_accum, lay.dq_rows, a.dq_sem, 4 * lay.ntq, domT, lse,
+                         lse_sh)
+            : launch_pdl(bwd_preprocess_sm100_kernel<T, 64, 64>,
+                         dim3((unsigned)((lay.dq_rows + 31) / 32), gy), dim3(256), 0, st, p, out,
+                         dout, delta, a.dq_accum, lay.dq_rows, a.dq_sem, 4 * lay.ntq, domT, lse,
+                         lse_sh);
+    if (e != cudaSuccess) return SSA_ERR_LAUNCH;
     note_launches(1);
   }
   // dQ accumulator as a 2-D fp32 tensor [rows][64] for the drain's tiled reduce-adds:
@@ -1709,8 +1696,10 @@ int run_bwd128(const Problem& p, TensorRef q, TensorRef k, TensorRef v, TensorRe
                    : nullptr;
   {
     dim3 gp((unsigned)((lay.dq_rows + 15) / 16), p.cu_seqlens ? p.Hq : p.B * p.Hq);
-    bwd_preprocess_sm100_kernel<T, 128, 128><<<gp, 256, 0, st>>>(
-        p, out, dout, delta, a.dq_accum, lay.dq_rows, a.dq_sem, 4 * lay.ntq, domT, lse, lse_sh);
+    if (launch_pdl(bwd_preprocess_sm100_kernel<T, 128, 128>, gp, dim3(256), 0, st, p, out, dout,
+                   delta, a.dq_accum, lay.dq_rows, a.dq_sem, 4 * lay.ntq, domT, lse,
+                   lse_sh) != cudaSuccess)
+      return SSA_ERR_LAUNCH;
   }
   {  // dQ accumulator as 2-D fp32 [rows][128]; {32 head dims x 64 queries} boxes, no swizzle
     auto enc = tmap_encoder();

@@ -104,6 +104,12 @@ __global__ void __launch_bounds__(192, 2)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const Problem& p = a.p;
+  // Launched programmatically: the grid may be dispatched while the previous kernel on the stream
+  // still runs, and waits here, before any global access (inputs that kernel may write, outputs in
+  // memory it may still read, the status word it may set). The next kernel may launch as soon as
+  // every CTA of this grid has started; it waits for this grid the same way.
+  griddep_wait();
+  griddep_launch_dependents();
   const int BH = p.B * p.Hq;
   const int tile = a.tiles_m - 1 - (int)(blockIdx.x / BH);  // longest causal rows first
   const int bh = blockIdx.x % BH;
@@ -471,7 +477,9 @@ int run_fwd(const Problem& p, TensorRef q, TensorRef k, TensorRef v, TensorRef o
   if (set_smem_limit_once(reinterpret_cast<const void*>(kern), (int)C::SMEM_BYTES) != SSA_OK)
     return SSA_ERR_CUDA;
   const long long grid = (long long)a.tiles_m * p.B * p.Hq;
-  kern<<<(unsigned)grid, C::THREADS, C::SMEM_BYTES, st>>>(tq, tk, tv, a);
+  if (launch_pdl(kern, dim3((unsigned)grid), dim3(C::THREADS), C::SMEM_BYTES, st, tq, tk, tv, a) !=
+      cudaSuccess)
+    return SSA_ERR_LAUNCH;
   note_launches(1);
   return SSA_OK;
 }

@@ -1736,6 +1736,10 @@ int launch_bwd_sm100(int dtype, const Problem& p, TensorRef q, TensorRef k, Tens
                      TensorRef out, TensorRef dout, const float* lse, float* delta, TensorRef dq,
                      TensorRef dk, TensorRef dv, float* dn, float* db, void* dom, void* ws,
                      size_t ws_bytes, cudaStream_t st) {
+  // The dQ accumulator's reduce-adds address its rows with 32-bit TMA coordinates.
+  const sm100::BwdLayout lay = sm100::bwd_layout(p);
+  if ((int64_t)(p.cu_seqlens ? p.Hq : p.B * p.Hq) * lay.dq_rows >= (int64_t)1 << 31)
+    return SSA_ERR_BAD_SHAPE;
   if (p.D == 128)
     return dtype == SSA_DTYPE_BF16
                ? sm100::run_bwd128<true>(p, q, k, v, out, dout, lse, delta, dq, dk, dv, dn, db,

@@ -1,10 +1,13 @@
 """Megatron GPT layer spec with SSA core attention (drop-in for the reference's
 ``SSA.ssa_triton_layer_specs``, training/train/train_ssa_triton/SSA/ssa_triton_layer_specs.py).
 
-Same layer-spec function and signature. Megatron-core is imported lazily, so importing this
-module works without it; building a spec needs it. The residual bias-dropout-add is Megatron's
-own (``megatron.core.fusions.fused_bias_dropout.get_bias_dropout_add``), optionally compiled with
-``torch.compile`` as the reference does (``SSA_TRITON_COMPILE_BDA``, default on).
+Same layer-spec function and signature, and the same bias-dropout-add factories
+(``get_bias_dropout_add``, ``get_compiled_bias_dropout_add``, reference :27-60). Megatron-core
+is imported lazily, so importing this module works without it; building a spec needs it. The
+residual bias-dropout-add is Megatron's own
+(``megatron.core.fusions.fused_bias_dropout.get_bias_dropout_add``) when megatron-core is
+importable, optionally compiled with ``torch.compile`` as the reference does
+(``SSA_TRITON_COMPILE_BDA``, default on).
 """
 
 from __future__ import annotations
@@ -16,17 +19,36 @@ from typing import Optional
 from .ssa_triton_attention import SSATritonAttention
 
 
-def _compiled_bda_factory(training, fused):
-    """Bias-dropout-add factory for ``use_compiled_bda`` (the reference compiles its unfused
-    bias-dropout-add with ``torch.compile``, ssa_triton_layer_specs.py:45-60): Megatron's own
-    unfused function for ``training``, compiled once per flag."""
+def _residual_dropout(training: bool, x_with_bias, residual, prob: float):
+    """residual + dropout(x + bias): the TransformerLayer's bias-dropout-add contract, eager."""
+    import torch.nn.functional as F
+    x, bias = x_with_bias
+    if bias is not None:
+        x = x + bias
+    return residual + (F.dropout(x, p=prob, training=True) if training and prob > 0.0 else x)
+
+
+def get_bias_dropout_add(training, fused_bias_dropout_add):
+    """Bias-dropout-add factory with the reference's signature (ssa_triton_layer_specs.py:27-42):
+    a function (x_with_bias, residual, prob) -> residual + dropout(x + bias). Megatron's own
+    factory when megatron-core is importable, else the eager equivalent."""
+    try:
+        from megatron.core.fusions.fused_bias_dropout import get_bias_dropout_add as mcore_bda
+    except ImportError:
+        return functools.partial(_residual_dropout, bool(training))
+    return mcore_bda(training, fused_bias_dropout_add)
+
+
+def get_compiled_bias_dropout_add(training, fused_bias_dropout_add):
+    """The unfused bias-dropout-add of :func:`get_bias_dropout_add` compiled with
+    ``torch.compile`` once per ``training`` flag (reference :45-60); the eager function when no
+    compiler backend is available."""
     return _compiled_bda(bool(training))
 
 
 @functools.lru_cache(maxsize=None)
 def _compiled_bda(training: bool):
     import torch
-    from megatron.core.fusions.fused_bias_dropout import get_bias_dropout_add
     eager = get_bias_dropout_add(training, False)
     try:
         return torch.compile(eager, mode="reduce-overhead")
@@ -50,11 +72,9 @@ def get_ssa_triton_gpt_layer_spec(num_experts: Optional[int] = None,
     from megatron.core.transformer.transformer_layer import (TransformerLayer,
                                                              TransformerLayerSubmodules)
 
-    from megatron.core.fusions.fused_bias_dropout import get_bias_dropout_add
-
     if use_compiled_bda is None:
         use_compiled_bda = os.environ.get("SSA_TRITON_COMPILE_BDA", "1") != "0"
-    bda_factory = _compiled_bda_factory if use_compiled_bda else get_bias_dropout_add
+    bda_factory = get_compiled_bias_dropout_add if use_compiled_bda else get_bias_dropout_add
     mlp = _get_mlp_module_spec(num_experts=num_experts, moe_grouped_gemm=moe_grouped_gemm)
     core = ModuleSpec(module=SSATritonAttention,
                       params={"ssa_n": ssa_n, "ssa_b": ssa_b, "learnable_ssa": learnable_ssa,

@@ -139,6 +139,30 @@ def test_layer_spec_requires_megatron_only_when_called():
             ls.get_ssa_triton_gpt_layer_spec()
 
 
+def test_bias_dropout_add_factories():
+    """The reference's bias-dropout-add factories exist with its signatures; without Megatron the
+    eager function computes residual + dropout(x + bias), with dropout only in training."""
+    import SSA.ssa_triton_layer_specs as ls
+    g = torch.Generator().manual_seed(0)
+    x, bias, res = (torch.randn(4, 8, generator=g) for _ in range(3))
+    try:
+        import megatron  # noqa: F401
+        have_megatron = True
+    except ImportError:
+        have_megatron = False
+    eval_fn = ls.get_bias_dropout_add(False, False)
+    assert torch.allclose(eval_fn((x, bias), res, 0.5), x + bias + res)
+    assert torch.allclose(eval_fn((x, None), res, 0.0), x + res)
+    if not have_megatron:
+        train_fn = ls.get_bias_dropout_add(True, False)
+        y = train_fn((x, bias), res, 0.5) - res
+        kept = y != 0
+        assert kept.any() and (~kept).any()
+        assert torch.allclose(y[kept], 2.0 * (x + bias)[kept])
+    assert ls.get_compiled_bias_dropout_add(True, False) is ls.get_compiled_bias_dropout_add(True, True)
+    assert callable(ls.get_compiled_bias_dropout_add(False, False))
+
+
 def test_missing_library_fails_loudly():
     """No CPU or PyTorch fallback: without libssa_b200.so every entry point raises."""
     import subprocess

@@ -616,11 +616,13 @@ def main():
     pending = []
     with ClockSampler(local, deferred=True) as clk:
         barrier()
-        # A device-side wait of ~0.5 ms ahead of the start event lets the host queue the first
+        # A device-side wait of ~2 ms ahead of the start event lets the host queue the first
         # steps before the device reaches them, as in a training loop's steady state; without it
         # the first timed step also carries the host's launch latency (~0.1 ms, 4% of a 20-step
-        # region at 8 GPUs). The timed region still holds exactly the K steps.
-        torch.cuda._sleep(1_000_000)
+        # region at 8 GPUs), and a host thread delayed early in the region (by the OS, on a host
+        # running one process per GPU) idles every rank through the collective. The timed region
+        # still holds exactly the K steps.
+        torch.cuda._sleep(4_000_000)
         start.record(st)
         for i in range(args.steps):
             step(pending, ev[i])

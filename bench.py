@@ -1,5 +1,5 @@
 #!/usr/bin/env python3
-"""SSA attention fwd+bwd benchmark on B200, one process per GPU.
+"""SSA attention fwd+bwd benchmark (benchmark config 2) on B200, one process per GPU.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
     (N > 1: python -m torch.distributed.run --nproc-per-node N ... bench.py --gpus N ...)
@@ -45,7 +45,7 @@ for _p in (str(REPO), str(REPO / "luciole-1b_b200")):
 
 import torch  # noqa: E402
 
-# Workloads. c2 is the headline and the default; c3 / c4 are measured with
+# Workloads (the benchmark configs). c2 is the headline and the default; c3 / c4 are measured with
 # --config for the record. c3: packed documents, lengths seeded uniform in [128, 4096] until
 # 65,536 tokens (last one clipped); c4: one 32,768-token sequence at D = 128.
 CONFIGS = {
@@ -362,7 +362,7 @@ def _one_ref_step(threads):
 
 
 def run_train(args):
-    """one Luciole-1B-shaped training step per timed step (forward, loss,
+    """Benchmark config 5: one Luciole-1B-shaped training step per timed step (forward, loss,
     backward with DDP's gradient all-reduce, AdamW on fp32 masters) on random token ids,
     sequence 2048, micro-batch 4 per GPU. value = tokens/s of the whole job."""
     import luciole_train as LT

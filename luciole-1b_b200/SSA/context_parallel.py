@@ -1,4 +1,4 @@
-"""Context-parallel (ring) SSA attention for long sequences.
+"""Context-parallel (ring) SSA attention for long sequences (benchmark config 4).
 
 No reference counterpart: the reference asserts context parallelism off for SSA
 (training/train/train_ssa_triton/SSA/ssa_triton_attention.py:74-76). This module adds it with

@@ -1,4 +1,4 @@
-"""Luciole-1B-shaped training step over the SSA kernels.
+"""Luciole-1B-shaped training step over the SSA kernels (benchmark config 5).
 
 The caller of the SSA path in the reference is a NeMo / Megatron GPT decoder built from
 ``get_ssa_triton_gpt_layer_spec`` (training/train/train_ssa_triton/train_ssa_triton.py:401-413,

@@ -1,4 +1,4 @@
-"""GPU parity at the benchmarked sizes: the kernels run over whole BASELINE workloads (configs 2,
+"""GPU parity at the benchmarked sizes: the kernels run over whole benchmark workloads (configs 2,
 3 and 4) and slices of their outputs are checked against the blocked fp64 oracle
 (oracle.ssa_oracle.ssa_reference_grads_blocked, itself pinned to the autograd oracle on the CPU).
 

@@ -244,7 +244,7 @@ def test_backward_on_a_thread_without_cuda_context(cuda_device):
 
 
 def test_fp32_generic_path(cuda_device):
-    """fp32 within 1e-5 relative (BASELINE config 1 shape, reduced batch*heads)."""
+    """fp32 within 1e-5 relative (benchmark config 1 shape, reduced batch*heads)."""
     q = seeded((1, 4, 512, 64), 21, 1.0, torch.float32)
     k = seeded((1, 4, 512, 64), 22, 1.0, torch.float32)
     v = seeded((1, 4, 512, 64), 23, 1.0, torch.float32)
@@ -508,7 +508,7 @@ def test_autograd_function_and_module(cuda_device):
 
 
 def test_config2_full_size_slice(cuda_device):
-    """BASELINE config 2 shape (B=8, Hq=32, Hkv=8, S=2048, D=64, bf16, causal, per-head n). The
+    """benchmark config 2 shape (B=8, Hq=32, Hkv=8, S=2048, D=64, bf16, causal, per-head n). The
     (batch, kv-group) units are independent, so one unit's 4 q-heads are checked exactly against
     the fp64 oracle at full sequence length."""
     B, Hq, Hkv, N, D = 8, 32, 8, 2048, 64

@@ -89,7 +89,7 @@ def test_oracle_varlen_is_per_document():
 
 
 def test_flop_convention():
-    # E = 8*32*2048^2/2 = 5.369e8, FLOPs = 14*64*E = 4.810e11
+    # benchmark config 2: E = 8*32*2048^2/2 = 5.369e8, FLOPs = 14*64*E = 4.810e11
     assert causal_score_elements(8, 32, 2048, True) == 536870912
     assert math.isclose(attn_flops_fwd_bwd(8, 32, 2048, 64, True), 4.810e11, rel_tol=1e-3)
 

@@ -13,6 +13,13 @@ stream, overlapped with compute). For each q-chunk i and k-chunk j a rank comput
 attention of the pair (non-causal if j < i, causal if j == i, skipped if j > i) with the
 single-GPU kernels, and merges the partial (O, lse) results in base 2:
     lse = log2(sum_j 2^lse_j),  O = sum_j 2^(lse_j - lse) O_j
+The 2g+1 visible pairs of a rank run as g launches. At step 0 (its own K/V) the three pairs are
+one causal attention over the rank's two chunks in local order: local order agrees with global
+order for every visible pair, and the pair the mask hides (chunk r against chunk 2g-1-r) is the
+one causality removes. At every later step the two visible pairs share a key chunk (K/V from a
+lower rank: both of this rank's q-chunks see its first chunk) or a query chunk (K/V from a higher
+rank: the second q-chunk sees both of its chunks), and run as one non-causal launch with the two
+pairs stacked in the batch dimension.
 Backward: K/V travel again together with their dK/dV accumulators, which end on the owner
 after g hops; every pair's gradients use the FINAL out and lse (the base-2 normaliser of the
 whole row), so P = exp2(t2 - lse) and delta = rowsum(O dO) are those of full attention.
@@ -81,6 +88,25 @@ def _merge(o_acc, lse_acc, o_j, lse_j):
     return o_acc * w_old + o_j.to(dt) * w_new, lse
 
 
+def _stack_chunks(x: torch.Tensor, c: int) -> torch.Tensor:
+    """[B, H, 2c, ...] -> [2B, H, c, ...]: the first chunk's batch entries, then the second's.
+    A strided view when B == 1 and x is contiguous (the kernels take B/H/N strides), else a copy."""
+    if x.shape[0] == 1 and x.is_contiguous():
+        return x.unflatten(2, (2, c)).movedim(2, 0).squeeze(1)
+    return torch.cat([x[:, :, :c], x[:, :, c:]], dim=0)
+
+
+def _twice(x: torch.Tensor) -> torch.Tensor:
+    """[B, ...] -> [2B, ...]: two copies of the same batch entries."""
+    return torch.cat([x, x], dim=0)
+
+
+def _halves(x: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+    """[2B, ...] -> the first and second B entries."""
+    b = x.shape[0] // 2
+    return x[:b], x[b:]
+
+
 class _Ring:
     """One send/recv hop of a list of tensors around the ring (prev -> self -> next)."""
 
@@ -125,7 +151,6 @@ def ring_ssa_forward(q, k, v, softmax_scale, ssa_n, ssa_b, group=None,
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
     c = q.shape[2] // 2
-    my = zigzag_chunks(world, rank)
     qs = (q[:, :, :c], q[:, :, c:])
     acc_o = [None, None]
     acc_l = [None, None]
@@ -133,17 +158,22 @@ def ring_ssa_forward(q, k, v, softmax_scale, ssa_n, ssa_b, group=None,
     kv = [k, v]
     for step in range(world):
         src = (rank - step) % world
-        kchunks = zigzag_chunks(world, src)
         pending = ring.start(kv) if step + 1 < world else None
-        kk = (kv[0][:, :, :c], kv[0][:, :, c:])
-        vv = (kv[1][:, :, :c], kv[1][:, :, c:])
-        for qi in range(2):
-            for kj in range(2):
-                i, j = my[qi], kchunks[kj]
-                if j > i:
-                    continue
-                o_ij, l_ij = pair_fwd(qs[qi], kk[kj], vv[kj], softmax_scale, ssa_n, ssa_b, j == i)
-                acc_o[qi], acc_l[qi] = _merge(acc_o[qi], acc_l[qi], o_ij, l_ij)
+        if src == rank:  # own chunks: one causal attention over the local order
+            o, l = pair_fwd(q, kv[0], kv[1], softmax_scale, ssa_n, ssa_b, True)
+            parts = [(0, o[:, :, :c], l[:, :, :c]), (1, o[:, :, c:], l[:, :, c:])]
+        elif src < rank:  # both q-chunks against the sender's first chunk
+            o, l = pair_fwd(_stack_chunks(q, c), _twice(kv[0][:, :, :c]),
+                            _twice(kv[1][:, :, :c]), softmax_scale, ssa_n, ssa_b, False)
+            (o0, o1), (l0, l1) = _halves(o), _halves(l)
+            parts = [(0, o0, l0), (1, o1, l1)]
+        else:  # the second q-chunk against both of the sender's chunks
+            o, l = pair_fwd(_twice(qs[1]), _stack_chunks(kv[0], c), _stack_chunks(kv[1], c),
+                            softmax_scale, ssa_n, ssa_b, False)
+            (o0, o1), (l0, l1) = _halves(o), _halves(l)
+            parts = [(1, o0, l0), (1, o1, l1)]
+        for qi, o_p, l_p in parts:
+            acc_o[qi], acc_l[qi] = _merge(acc_o[qi], acc_l[qi], o_p, l_p)
         if pending is not None:
             kv = ring.finish(pending)
     out = torch.cat([acc_o[0], acc_o[1]], dim=2).to(q.dtype)
@@ -159,7 +189,6 @@ def ring_ssa_backward(q, k, v, out, dout, lse, softmax_scale, ssa_n, ssa_b, grou
     world = dist.get_world_size(group)
     rank = dist.get_rank(group)
     c = q.shape[2] // 2
-    my = zigzag_chunks(world, rank)
     qs = (q[:, :, :c], q[:, :, c:])
     os_ = (out[:, :, :c], out[:, :, c:])
     dos = (dout[:, :, :c], dout[:, :, c:])
@@ -175,24 +204,40 @@ def ring_ssa_backward(q, k, v, out, dout, lse, softmax_scale, ssa_n, ssa_b, grou
            torch.zeros(v.shape, dtype=acc, device=v.device)]
     for step in range(world):
         src = (rank - step) % world
-        kchunks = zigzag_chunks(world, src)
         # K/V for the next step can move now; the accumulators only after this step's adds
         pending_kv = ring.start(kv) if step + 1 < world else None
-        kk = (kv[0][:, :, :c], kv[0][:, :, c:])
-        vv = (kv[1][:, :, :c], kv[1][:, :, c:])
-        for qi in range(2):
-            for kj in range(2):
-                i, j = my[qi], kchunks[kj]
-                if j > i:
-                    continue
-                dq_ij, dk_ij, dv_ij, dn_ij, db_ij = pair_bwd(
-                    qs[qi], kk[kj], vv[kj], os_[qi], dos[qi], ls[qi], softmax_scale, ssa_n, ssa_b,
-                    j == i)
-                dq[:, :, qi * c:(qi + 1) * c] += dq_ij.to(acc)
-                dkv[0][:, :, kj * c:(kj + 1) * c] += dk_ij.to(acc)
-                dkv[1][:, :, kj * c:(kj + 1) * c] += dv_ij.to(acc)
-                dn += dn_ij.to(acc).reshape(dn.shape)
-                db += db_ij.to(acc).reshape(())
+        if src == rank:  # own chunks: one causal attention over the local order
+            dq_p, dk_p, dv_p, dn_p, db_p = pair_bwd(q, kv[0], kv[1], out, dout, lse.contiguous(),
+                                                    softmax_scale, ssa_n, ssa_b, True)
+            dq += dq_p.to(acc)
+            dkv[0] += dk_p.to(acc)
+            dkv[1] += dv_p.to(acc)
+        elif src < rank:  # both q-chunks against the sender's first chunk
+            dq_p, dk_p, dv_p, dn_p, db_p = pair_bwd(
+                _stack_chunks(q, c), _twice(kv[0][:, :, :c]), _twice(kv[1][:, :, :c]),
+                _stack_chunks(out, c), _stack_chunks(dout, c), _stack_chunks(lse, c).contiguous(),
+                softmax_scale, ssa_n, ssa_b, False)
+            dq0, dq1 = _halves(dq_p)
+            dq[:, :, :c] += dq0.to(acc)
+            dq[:, :, c:] += dq1.to(acc)
+            dk0, dk1 = _halves(dk_p)
+            dv0, dv1 = _halves(dv_p)
+            dkv[0][:, :, :c] += dk0.to(acc) + dk1.to(acc)
+            dkv[1][:, :, :c] += dv0.to(acc) + dv1.to(acc)
+        else:  # the second q-chunk against both of the sender's chunks
+            dq_p, dk_p, dv_p, dn_p, db_p = pair_bwd(
+                _twice(qs[1]), _stack_chunks(kv[0], c), _stack_chunks(kv[1], c), _twice(os_[1]),
+                _twice(dos[1]), _twice(ls[1]), softmax_scale, ssa_n, ssa_b, False)
+            dq0, dq1 = _halves(dq_p)
+            dq[:, :, c:] += dq0.to(acc) + dq1.to(acc)
+            dk0, dk1 = _halves(dk_p)
+            dv0, dv1 = _halves(dv_p)
+            dkv[0][:, :, :c] += dk0.to(acc)
+            dkv[0][:, :, c:] += dk1.to(acc)
+            dkv[1][:, :, :c] += dv0.to(acc)
+            dkv[1][:, :, c:] += dv1.to(acc)
+        dn += dn_p.to(acc).reshape(dn.shape)
+        db += db_p.to(acc).reshape(())
         # dK/dV follow their K/V chunk; after `world` hops they are back on the owner
         pending_d = ring.start(dkv)
         if pending_kv is not None:
